@@ -1,0 +1,356 @@
+"""Benchmark of the action-expert Euler loop, steps 2-10 (BASELINE.json metric):
+"action-expert ms per predict (steps 2-10, batch 1, 1xB200); episodes/s at 1/2/4/8 GPUs".
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl mk|reference]
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \
+        --master-port P bench.py --gpus N --steps K --warmup W
+
+One step = one predict's Euler steps 2..10 for one episode (REKI's expert,
+bf16, batch 1, T = 10 action rows, 2 of 3 register frames valid, 160 cross-attention source rows),
+replayed as a CUDA graph like the reference's own timing (src/profile_breakdown.py:107-130).
+Multi-GPU: one process per GPU, each serving its own episodes with its own weights copy, no
+collective (the path does not shard); value = episodes/s summed over ranks, from the max over
+ranks of the per-step device time.
+
+``--impl reference`` times the reference algorithm's CPU implementation on this host's cores: the
+repo's CPU oracle in fp32 (Kyutai's eager expert is not available here; the oracle restates it),
+rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "action-expert ms per predict (steps 2–10, batch 1, 1×B200); episodes/s at 1/2/4/8 GPUs"
+PUBLISHED_MS = 4.00          # reference megakernel v5, steps 2-10, 1x B200 (results/gpus/b200/test_mk.json:16)
+HBM_FALLBACK_GBS = 6650.0
+L2_FLUSH_BYTES = 256 << 20
+
+
+def algorithmic_bytes_per_step(dims, mods_row_bytes: int) -> int:
+    """HBM bytes one Euler step must stream: bf16 weights + fp32 in/out projections + norm weights +
+    one modulation row (BASELINE.md roofline figures)."""
+    L, H, I, A, HD = dims.L, dims.H, dims.I, dims.A, dims.HD
+    bf16 = 2 * L * (3 * H * H + 3 * H * H + 3 * H * I)
+    fp32 = 4 * (2 * A * H)
+    norms = 2 * 3 * L * HD
+    return bf16 + fp32 + norms + mods_row_bytes
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return HBM_FALLBACK_GBS, "fallback"
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region (SM clock, throttle reasons)."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"mkx_clocks_{os.getpid()}.csv"
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.idx), "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.f.close()
+        rows = [r.split(",") for r in self.path.read_text().splitlines() if r.strip()]
+        self.path.unlink(missing_ok=True)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+                for n, v in zip(names, r[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                continue
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def traffic_from_profile():
+    """dram bytes (read + write) per launch of expert_kernel, from the committed ncu summary."""
+    p = ROOT / "profiles" / "expert_kernel_full.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+# ------------------------------------------------------------------------------------------------
+def cpu_oracle_time(dims, seconds: float, threads: int):
+    """fp32 eager CPU expert (the oracle), one Euler step at a time on this host's cores; returns
+    (ms per predict = 9 Euler steps, Euler steps run, threads)."""
+    from oracle.expert_oracle import OracleExpert
+    from reki_megakernel_b200.synthetic import make_inputs, make_weights
+    torch.set_num_threads(threads)
+    w = make_weights(dims, seed=0)
+    orc = OracleExpert(w, "fp32")
+    inp = make_inputs(dims, n_steps=1)
+    e = inp.episode(0)
+    ep = dict(x=e.x[0], mods=e.mods[0], dt=e.dt[0], memk=e.memk[0], memv=e.memv[0], kv_start=int(e.kv_start[0]),
+              kca=e.kca[0], vca=e.vca[0], S=int(e.S[0]), sa_cos=e.sa_cos[0], sa_sin=e.sa_sin[0],
+              ca_cos=e.ca_cos[0], ca_sin=e.ca_sin[0], action_dim=inp.action_dim)
+    orc.run_episode(ep)  # warm-up
+    n, t0 = 0, time.perf_counter()
+    times = []
+    while time.perf_counter() - t0 < seconds or n < 3:
+        a = time.perf_counter()
+        orc.run_episode(ep)
+        times.append(time.perf_counter() - a)
+        n += 1
+    return 9 * statistics.median(times) * 1e3, n, threads
+
+
+def run_reference(args, rank: int, world: int):
+    if rank != 0:
+        return
+    from reki_megakernel_b200.synthetic import ExpertDims
+    dims = ExpertDims()
+    threads = len(os.sched_getaffinity(0))
+    # --warmup / --steps count Euler steps of the CPU expert here (each ~0.1-1 s); a predict is 9.
+    from oracle.expert_oracle import OracleExpert
+    from reki_megakernel_b200.synthetic import make_inputs, make_weights
+    torch.set_num_threads(threads)
+    orc = OracleExpert(make_weights(dims, seed=0), "fp32")
+    inp = make_inputs(dims, n_steps=1)
+    e = inp.episode(0)
+    ep = dict(x=e.x[0], mods=e.mods[0], dt=e.dt[0], memk=e.memk[0], memv=e.memv[0], kv_start=int(e.kv_start[0]),
+              kca=e.kca[0], vca=e.vca[0], S=int(e.S[0]), sa_cos=e.sa_cos[0], sa_sin=e.sa_sin[0],
+              ca_cos=e.ca_cos[0], ca_sin=e.ca_sin[0], action_dim=inp.action_dim)
+    for _ in range(args.warmup):
+        orc.run_episode(ep)
+    steps = min(args.steps, args.max_ref_steps)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        orc.run_episode(ep)
+    el = time.perf_counter() - t0
+    ms_predict = 9 * el / steps * 1e3
+    value = 1000.0 / ms_predict
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "episodes/s", "n_gpus": args.gpus,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": ms_predict, "ms_per_predict": ms_predict,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "REKI expert steps 2-10, batch 1 (BASELINE configs[1] shapes), CPU fp32 eager",
+                   "T": 10, "S": 160, "memory_rows": 64, "euler_steps": 9},
+        "cpu_baseline": {"value": value, "unit": "episodes/s", "cores": threads, "kind": "port",
+                         "sample": f"{steps} Euler steps of one episode (x9 = ms per predict), fp32 oracle"},
+        "e2e": {"value": value, "unit": "episodes/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------------
+def run_mk(args, rank: int, world: int):
+    from reki_megakernel_b200.mk_expert import ExpertMegakernel
+    from reki_megakernel_b200.synthetic import ExpertDims, make_inputs, make_past, make_weights
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dims = ExpertDims()
+    w = make_weights(dims, seed=0)
+    mk = ExpertMegakernel(weights=w.to(dev))
+    del w
+    # this rank's episodes: seeds by global episode index
+    ep0 = rank * args.batch
+    inp = make_inputs(dims, seed=ep0, noise_seed=1234 + ep0).to(dev)
+    past = make_past(inp)
+    x1, mods, dt = inp.x[:1], inp.mods[0], inp.dt[:1]
+
+    def call():
+        return mk.run(x1, mods, dt, past, inp.action_dim)
+
+    # CUDA graph of one predict's steps 2..10, as the expert graph holds it in production
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        for _ in range(2):
+            call()
+    torch.cuda.current_stream(dev).wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = call()
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    for _ in range(args.warmup):
+        g.replay()
+    torch.cuda.synchronize(dev)
+    mk.check_device_error()
+    clocks = Clocks(local)
+    clocks.start()
+    time.sleep(0.3)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize(dev)
+    t_wall = time.perf_counter()
+    for a, b in evs:
+        flush.fill_(1)              # L2 flush between timed steps (not timed)
+        a.record(stream)
+        g.replay()
+        b.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    wall = time.perf_counter() - t_wall
+    clk = clocks.stop()
+    mk.check_device_error()
+    per = [a.elapsed_time(b) for a, b in evs]
+    ms = statistics.mean(per)
+    # end to end through the public API: H2D of every per-call input from pinned host memory,
+    # the launch, D2H of the result; timed with events on the stream
+    from types import SimpleNamespace
+    rs = past.register_step
+    dev_in = {"x": x1, "mods": mods, "dt": dt, "memk": inp.memk[0], "memv": inp.memv[0], "kca": inp.kca[0],
+              "vca": inp.vca[0], "cu_kv": rs["cu_kv"], "cu_src": rs["cu_src"], "sa_cos": inp.sa_cos[0],
+              "sa_sin": inp.sa_sin[0], "ca_cos": inp.ca_cos[0], "ca_sin": inp.ca_sin[0]}
+    host = {k: v.cpu().contiguous().pin_memory() for k, v in dev_in.items()}
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    out_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    d2h = out_host.numel() * out_host.element_size()
+    bufs = {k: torch.empty_like(v, device=dev) for k, v in host.items()}
+    past_b = SimpleNamespace(
+        register_step={"mem_kv": [(bufs["memk"][l], bufs["memv"][l]) for l in range(dims.L)],
+                       "sa_pe": (bufs["sa_cos"], bufs["sa_sin"]), "ca_pe": (bufs["ca_cos"], bufs["ca_sin"]),
+                       "cu_kv": bufs["cu_kv"], "cu_src": bufs["cu_src"]},
+        cross_attn_kv=[(bufs["kca"][l], bufs["vca"][l]) for l in range(dims.L)])
+
+    def e2e_call():
+        for k in host:
+            bufs[k].copy_(host[k], non_blocking=True)
+        o = mk.run(bufs["x"], bufs["mods"], bufs["dt"], past_b, inp.action_dim)
+        out_host.copy_(o, non_blocking=True)
+
+    for _ in range(max(3, args.warmup // 4)):
+        e2e_call()
+    torch.cuda.synchronize(dev)
+    n_e2e = max(10, args.steps // 4)
+    e2e_ms = []
+    for _ in range(n_e2e):
+        flush.fill_(1)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        e2e_call()
+        b.record(stream)
+        b.synchronize()
+        e2e_ms.append(a.elapsed_time(b))
+    mk.check_device_error()
+    e2e_mean = statistics.mean(e2e_ms)
+
+    # max over ranks
+    t = torch.tensor([ms, e2e_mean], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms_max, e2e_max = float(t[0]), float(t[1])
+    if rank != 0:
+        return
+    hbm, peak_kind = peaks()
+    mods_row = dims.MODW * 2
+    bytes_step = algorithmic_bytes_per_step(dims, mods_row)
+    achieved = 9 * bytes_step / (ms * 1e-3) / 1e9
+    value = world * args.batch * 1000.0 / ms_max
+    line = {
+        "metric": METRIC, "value": value, "unit": "episodes/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_max, "ms_per_predict": ms_max,
+        "ms_per_predict_p50": statistics.median(per), "ms_per_predict_p99": sorted(per)[min(len(per) - 1, int(0.99 * len(per)))],
+        "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": (1000.0 / ms_max) / (1000.0 / PUBLISHED_MS),
+        "dtype": "bf16", "data": "synthetic (seeded N(0,0.02) weights, BASELINE configs[1] shapes)",
+        "config": {"workload": "REKI expert Euler steps 2-10, batch 1 per GPU (BASELINE configs[1])",
+                   "T": 10, "S": 160, "memory_rows": 64, "euler_steps": 9, "episodes_per_gpu": args.batch,
+                   "parallelism": f"replicas x{world}, no collective",
+                   "l2": "256 MB written between timed predicts (untimed); weights (212 MB/step) exceed L2",
+                   "timing": "CUDA-graph replay, CUDA events per predict, mean over steps, max over ranks"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_kind": f"{peak_kind} (hbm copy, burst)", "traffic": traffic_from_profile(),
+                     "algorithmic_bytes_per_launch": 9 * bytes_step},
+        "e2e": {"value": world * args.batch * 1000.0 / e2e_max, "unit": "episodes/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_predict": e2e_max},
+        "gpu_launches": args.steps,
+        "clocks": clk,
+        "wall_s_timed_region": wall,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        cpu_ms, n, thr = cpu_oracle_time(dims, args.cpu_seconds, len(os.sched_getaffinity(0)))
+        line["cpu_baseline"] = {"value": 1000.0 / cpu_ms, "unit": "episodes/s", "cores": thr, "kind": "port",
+                                "sample": f"{n} Euler steps of one episode, fp32 CPU oracle; x9 per predict",
+                                "ms_per_predict": cpu_ms}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="mk", choices=["mk", "reference"])
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--max-ref-steps", type=int, default=60)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        backend = "nccl" if args.impl == "mk" else "gloo"
+        if backend == "nccl":
+            torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        torch.distributed.init_process_group(backend, timeout=timedelta(seconds=120))
+    try:
+        if args.impl == "reference":
+            run_reference(args, rank, world)
+        else:
+            run_mk(args, rank, world)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,143 @@
+/*
+ * mkx.h -- C ABI of the B200 action-expert megakernel (REKI expert, Euler steps 2..N).
+ *
+ * Plain C: device pointers, sizes and a cudaStream_t; no torch types. Every entry point returns an
+ * mkx_status (0 = success). All pointers marked "device" must point to memory of the device the
+ * handle was created on.
+ *
+ * Reference interface each entry point replaces (project muninn-huginn/reki-megakernel):
+ *   mkx_create      <- ExpertMegakernel.__init__(model)            src/mk_expert.py:436-481
+ *   mkx_run         <- ExpertMegakernel.run(x_t, mods, dt, past, action_dim)
+ *                                                                  src/mk_expert.py:483-515
+ *   mkx_sync_points <- ExpertMegakernel.barriers(n_steps)          src/mk_expert.py:517-518
+ *   mkx_last_error  <- (stage counter) test_mk.py's read-back of the barrier counter, compared
+ *                      with nprog * barriers(n_steps)                    src/test_mk.py:43-45
+ *                      (error word) the reference has none: a broken grid barrier deadlocks
+ *                      (README.md:262-263); here every device-side wait is bounded and reports
+ *   mkx_destroy     <- Python object lifetime of ExpertMegakernel
+ *   mkx_set_timeout_ns, mkx_clear_error, mkx_set_fault_injection, mkx_launch_shape,
+ *   mkx_last_cuda_error <- no counterpart (bounded waits, their test hook, introspection)
+ */
+#ifndef MKX_H_
+#define MKX_H_
+
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MKX_MAX_LAYERS 16
+
+typedef int mkx_status;
+enum {
+  MKX_OK = 0,
+  MKX_ERR_INVALID_ARG = 1,   /* null pointer, bad shape, misaligned pointer */
+  MKX_ERR_UNSUPPORTED = 2,   /* geometry the kernel is not built for */
+  MKX_ERR_CUDA = 3,          /* a CUDA runtime call failed (see mkx_last_cuda_error) */
+  MKX_ERR_DEVICE = 4,        /* the kernel reported an error (timeout); see mkx_last_error */
+  MKX_ERR_RESOURCES = 5      /* not enough SMs / shared memory for a co-resident grid */
+};
+
+typedef struct mkx_handle mkx_handle;
+
+/* Expert geometry (REKI: L=10, H=768, NH=12, HD=64, I=3072, A=32). H, NH, HD are fixed by the
+ * kernel (768 / 12 / 64); L <= MKX_MAX_LAYERS; I a multiple of 128; 8 <= A <= 32. */
+typedef struct {
+  int L, H, NH, HD, I, A;
+  float eps;          /* AdaRMS epsilon (input_layernorm.eps == action_expert.norm.eps) */
+  float qk_eps;       /* per-head q/k RMSNorm epsilon */
+  int max_rows;       /* largest T (action rows) a run may use; <= 16 */
+  int grid;           /* CTAs of the persistent launch; 0 = one per SM */
+} mkx_dims;
+
+/* Expert weights in the reference's stacked layout (src/mk_expert.py:445-460); device pointers,
+ * row-major, read once by mkx_create (the handle keeps its own packed copy). */
+typedef struct {
+  const uint16_t* wqkv;   /* bf16 [L, 3H, H]  cat(q_proj, k_proj, v_proj) */
+  const uint16_t* wo;     /* bf16 [L, H, H]   self_attn.o_proj */
+  const uint16_t* wqca;   /* bf16 [L, H, H]   cross_attn.q_proj */
+  const uint16_t* woca;   /* bf16 [L, H, H]   cross_attn.o_proj */
+  const uint16_t* wg;     /* bf16 [L, I, H]   mlp.gate_proj */
+  const uint16_t* wu;     /* bf16 [L, I, H]   mlp.up_proj */
+  const uint16_t* wd;     /* bf16 [L, H, I]   mlp.down_proj */
+  const uint16_t* qn;     /* bf16 [L, HD]     self_attn.q_norm.weight (scale = 1 + w) */
+  const uint16_t* kn;     /* bf16 [L, HD]     self_attn.k_norm.weight */
+  const uint16_t* qcan;   /* bf16 [L, HD]     cross_attn.q_norm.weight */
+  const float* win;       /* fp32 [A, H]      action_in_proj.weight TRANSPOSED */
+  const float* bin;       /* fp32 [H]         action_in_proj.bias */
+  const float* wout;      /* fp32 [A, H]      action_out_proj.weight */
+  const float* bout;      /* fp32 [A]         action_out_proj.bias */
+} mkx_weights;
+
+/* Inputs of one call of Euler steps 2..N (batch 1). Device pointers unless noted. */
+typedef struct {
+  const float* x_in;      /* [T, A] fp32: action state after Euler step 1 */
+  float* x_out;           /* [T, A] fp32: action state after step N (padded dims: 0 + dt * v) */
+  const void* mods;       /* [N, MODW] per-step modulations, row 0 (step 1) unused; MODW = 9LH + 2H */
+  int mods_fp32;          /* 0: bf16 mods, 1: fp32 mods */
+  const float* dt;        /* [1] fp32 Euler step */
+  /* register memory K/V per layer: [PM, NH, HD] bf16 rows, valid rows [cu_kv[0], PM), already
+   * normed and rotated (past.register_step['mem_kv'][l]) */
+  const uint16_t* memk[MKX_MAX_LAYERS];
+  const uint16_t* memv[MKX_MAX_LAYERS];
+  int mem_rows;           /* PM */
+  int mem_row_stride;     /* elements between consecutive rows (NH*HD when contiguous) */
+  const int* cu_kv;       /* device int32; cu_kv[0] = first valid memory row */
+  /* cross-attention source K/V per layer: [SP, NH, HD] bf16, valid rows [0, cu_src[1]) */
+  const uint16_t* kca[MKX_MAX_LAYERS];
+  const uint16_t* vca[MKX_MAX_LAYERS];
+  int ca_rows;            /* SP: rows allocated per layer (the kernel reads min(cu_src[1], SP) rows) */
+  int ca_row_stride;      /* elements between consecutive rows */
+  const int* cu_src;      /* device int32; cu_src[1] = S valid source rows */
+  const float* sa_cos;    /* [T, HD] fp32 RoPE tables of the action rows (self-attention) */
+  const float* sa_sin;
+  const float* ca_cos;    /* [T, HD] fp32 RoPE tables of the action rows (cross-attention) */
+  const float* ca_sin;
+  int T;                  /* action rows, 1..max_rows */
+  int n_steps;            /* Euler steps to run (= N - 1), >= 1 */
+  int action_dim;         /* real action dims, 1..8 */
+  uint16_t* trace_h;      /* optional [n_steps, L, T, H] bf16: every layer's output h; may be NULL */
+} mkx_step_inputs;
+
+/* Packs the weights into the handle's own device memory (one-off, synchronous on `stream`'s
+ * device) and allocates the launch's scratch. */
+mkx_status mkx_create(const mkx_dims* dims, const mkx_weights* w, int device, mkx_handle** out);
+
+/* Enqueues one persistent launch for steps 2..N on `stream`. No host synchronisation, no host
+ * reads of device data: capturable in a CUDA graph. One launch in flight per handle. */
+mkx_status mkx_run(mkx_handle* h, const mkx_step_inputs* in, cudaStream_t stream);
+
+/* Number of dependent exchange points (the dataflow counterpart of grid barriers) per launch. */
+int mkx_sync_points(const mkx_handle* h, int n_steps);
+
+/* Reads (synchronously) the device status words: *code = 0 when every wait completed; otherwise
+ * an encoded (cta << 16 | kind << 8 | stage) of the first failed wait. *stages = sum over CTAs of
+ * the stages each CTA completed, accumulated over the launches since mkx_create or the last
+ * mkx_clear_error (one launch of n steps: grid * mkx_sync_points(n)). Either pointer may be NULL. */
+mkx_status mkx_last_error(mkx_handle* h, int* code, long long* stages);
+
+/* Clears the device error word and the stage counter (synchronous). */
+mkx_status mkx_clear_error(mkx_handle* h);
+
+/* Device-side wait limit in nanoseconds (default 2e9). */
+mkx_status mkx_set_timeout_ns(mkx_handle* h, unsigned long long ns);
+
+/* Test hook for the failure path (no GPU fault involved): with stage == 1, CTA 0 withholds its
+ * layer-0 QKV words in later launches, so the bounded waits on them run out and the launch reports
+ * MKX_ERR_DEVICE through mkx_last_error. 0 disables it. */
+mkx_status mkx_set_fault_injection(mkx_handle* h, int stage);
+
+/* Grid size actually used and dynamic shared memory bytes per CTA. */
+mkx_status mkx_launch_shape(const mkx_handle* h, int* grid, int* smem_bytes);
+
+/* Last CUDA error string seen by the library (thread-local, static storage). */
+const char* mkx_last_cuda_error(void);
+
+void mkx_destroy(mkx_handle* h);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MKX_H_ */

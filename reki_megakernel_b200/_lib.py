@@ -1,0 +1,98 @@
+"""ctypes binding of ``libmkx.so`` (declarations in ``include/mkx.h``).
+
+The library is built in-tree by ``reki_megakernel_b200.build``. There is no fallback: if the
+library is missing or does not load, importing this module raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+from . import build as _build
+
+MAX_LAYERS = 16
+
+MKX_OK, MKX_ERR_INVALID_ARG, MKX_ERR_UNSUPPORTED, MKX_ERR_CUDA, MKX_ERR_DEVICE, MKX_ERR_RESOURCES = range(6)
+STATUS_NAMES = {0: "OK", 1: "INVALID_ARG", 2: "UNSUPPORTED", 3: "CUDA", 4: "DEVICE", 5: "RESOURCES"}
+
+# Exported entry points and their ctypes signatures (restype, argtypes).
+P = C.c_void_p
+
+
+class Dims(C.Structure):
+    _fields_ = [("L", C.c_int), ("H", C.c_int), ("NH", C.c_int), ("HD", C.c_int), ("I", C.c_int),
+                ("A", C.c_int), ("eps", C.c_float), ("qk_eps", C.c_float), ("max_rows", C.c_int),
+                ("grid", C.c_int)]
+
+
+class Weights(C.Structure):
+    _fields_ = [(n, P) for n in ("wqkv", "wo", "wqca", "woca", "wg", "wu", "wd", "qn", "kn", "qcan",
+                                 "win", "bin", "wout", "bout")]
+
+
+class StepInputs(C.Structure):
+    _fields_ = [("x_in", P), ("x_out", P), ("mods", P), ("mods_fp32", C.c_int), ("dt", P),
+                ("memk", P * MAX_LAYERS), ("memv", P * MAX_LAYERS), ("mem_rows", C.c_int),
+                ("mem_row_stride", C.c_int), ("cu_kv", P),
+                ("kca", P * MAX_LAYERS), ("vca", P * MAX_LAYERS), ("ca_rows", C.c_int), ("ca_row_stride", C.c_int),
+                ("cu_src", P),
+                ("sa_cos", P), ("sa_sin", P), ("ca_cos", P), ("ca_sin", P),
+                ("T", C.c_int), ("n_steps", C.c_int), ("action_dim", C.c_int), ("trace_h", P)]
+
+
+SIGNATURES = {
+    "mkx_create": (C.c_int, [C.POINTER(Dims), C.POINTER(Weights), C.c_int, C.POINTER(P)]),
+    "mkx_run": (C.c_int, [P, C.POINTER(StepInputs), P]),
+    "mkx_sync_points": (C.c_int, [P, C.c_int]),
+    "mkx_last_error": (C.c_int, [P, C.POINTER(C.c_int), C.POINTER(C.c_longlong)]),
+    "mkx_clear_error": (C.c_int, [P]),
+    "mkx_set_timeout_ns": (C.c_int, [P, C.c_ulonglong]),
+    "mkx_set_fault_injection": (C.c_int, [P, C.c_int]),
+    "mkx_launch_shape": (C.c_int, [P, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+    "mkx_last_cuda_error": (C.c_char_p, []),
+    "mkx_destroy": (None, [P]),
+}
+
+_LIB = None
+
+
+def lib_path() -> Path:
+    return _build.LIB
+
+
+def load(build_if_missing: bool = True) -> C.CDLL:
+    """Load (building first if missing or stale and nvcc exists) the CUDA library."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    path = _build.LIB
+    if build_if_missing:
+        try:
+            if _build.stale():
+                _build.build()
+        except RuntimeError:
+            if not path.exists():
+                raise
+    if not path.exists():
+        raise ImportError(f"{path} is missing: run `python -m reki_megakernel_b200.build` (needs nvcc)")
+    lib = C.CDLL(str(path))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _LIB = lib
+    return lib
+
+
+class MkxError(RuntimeError):
+    def __init__(self, where: str, status: int, detail: str = ""):
+        self.status = status
+        super().__init__(f"{where} failed: {STATUS_NAMES.get(status, status)}" + (f" ({detail})" if detail else ""))
+
+
+def check(status: int, where: str) -> None:
+    if status != MKX_OK:
+        detail = ""
+        if status == MKX_ERR_CUDA:
+            detail = (load().mkx_last_cuda_error() or b"").decode(errors="replace")
+        raise MkxError(where, status, detail)

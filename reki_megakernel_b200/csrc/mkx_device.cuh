@@ -1,0 +1,133 @@
+// Device-side primitives of the expert megakernel: bounded waits on tagged L2 words, mbarriers,
+// bulk (TMA) copies global -> shared, bf16 tensor-core MMA, bf16 packing.
+#pragma once
+#include <stdint.h>
+#include <cuda_bf16.h>
+
+namespace mkx {
+
+typedef unsigned long long u64;
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---- exchange words: {payload u32 (low), tag u32 (high)}, 8-byte single-copy-atomic accesses ----
+__device__ __forceinline__ void ld_volatile_v2(const u64* p, u64& a, u64& b) {
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+__device__ __forceinline__ void st_volatile(u64* p, u64 v) {
+  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ int ld_volatile_i32(const int* p) {
+  int v;
+  asm volatile("ld.volatile.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint32_t tag_of(u64 w) { return (uint32_t)(w >> 32); }
+__device__ __forceinline__ uint32_t payload_of(u64 w) { return (uint32_t)w; }
+__device__ __forceinline__ u64 make_word(uint32_t tag, uint32_t payload) {
+  return ((u64)tag << 32) | (u64)payload;
+}
+
+// Position of column pair `kp` inside a row of exchange words: inside every block of 8 pairs the
+// order is 0,4,1,5,2,6,3,7, so the two pairs an MMA B fragment needs (kp, kp + 4) are adjacent.
+__host__ __device__ __forceinline__ int word_pos(int kp) {
+  return (kp & ~7) | ((kp & 3) << 1) | ((kp >> 2) & 1);
+}
+// Inverse of word_pos.
+__host__ __device__ __forceinline__ int word_pair(int pos) {
+  return (pos & ~7) | ((pos >> 1) & 3) | ((pos & 1) << 2);
+}
+
+// Bounded spin state: every 64th spin checks the launch's error word (another CTA gave up) and
+// the %globaltimer budget. tick(): 0 keep spinning, 1 timed out, 2 another CTA aborted.
+struct Waiter {
+  const int* err;
+  uint64_t t0;
+  uint64_t limit;
+  uint32_t spins;
+  __device__ __forceinline__ Waiter(const int* e, uint64_t lim) : err(e), t0(0), limit(lim), spins(0) {}
+  __device__ __forceinline__ int tick() {
+    ++spins;
+    if ((spins & 63u) != 0u) return 0;
+    if (ld_volatile_i32(err) != 0) return 2;
+    const uint64_t now = globaltimer();
+    if (t0 == 0) { t0 = now; return 0; }
+    return (now - t0 > limit) ? 1 : 0;
+  }
+};
+
+// ---- shared memory, mbarriers, bulk copies ----
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// 1D bulk copy (TMA engine) global -> this CTA's shared memory, completion counted in bytes on `bar`.
+// dst, src 16-byte aligned; bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+// Orders this thread's earlier generic-proxy shared-memory accesses before later async-proxy ones.
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ uint2 lds64(const void* p) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(smem_u32(p)));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds32(const void* p) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)));
+  return v;
+}
+
+// ---- tensor-core MMA: D[16 x 8] += A[16 x 16] (row) * B[16 x 8] (col), bf16 in, fp32 accumulate ----
+__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// ---- bf16 helpers (bf16 -> fp32 is exact; fp32 -> bf16 rounds to nearest even) ----
+__device__ __forceinline__ float bf_lo(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
+__device__ __forceinline__ float bf_at(uint16_t v) { return __uint_as_float(((uint32_t)v) << 16); }
+__device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
+  __nv_bfloat162 t = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&t);
+}
+__device__ __forceinline__ float round_bf(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+}  // namespace mkx

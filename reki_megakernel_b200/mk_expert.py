@@ -1,0 +1,218 @@
+"""Drop-in replacement for the reference's ``src/mk_expert.py`` (``ExpertMegakernel``, ``install``).
+
+Same names, arguments and behaviour as the reference launcher:
+
+* ``ExpertMegakernel(model)`` reads the expert from a REKI-shaped model object
+  (``src/mk_expert.py:436-481``), packs it once into the CUDA library's own device memory
+  (``mkx_create``) and keeps the reference's attributes (``L, NH, HD, H, I, A, TP, nprog, cfg``).
+* ``.run(x_t, mods, dt, past, action_dim)`` integrates Euler steps 2..N in one persistent launch on
+  the current stream and returns a fresh ``[1, T, A]`` fp32 tensor (``src/mk_expert.py:483-515``).
+  It reads ``past.register_step`` (``mem_kv``, ``sa_pe``, ``ca_pe``, ``cu_kv``, ``cu_src``) and
+  ``past.cross_attn_kv`` in place: the per-layer K/V tensors are passed by pointer, no stacking copy.
+  No host synchronisation happens, so the call can be captured in a CUDA graph (the reference's
+  launch sits inside Kyutai's expert graph).
+* ``.barriers(n_steps)`` keeps the reference's count ``1 + n_steps (8 L + 1)``
+  (``src/mk_expert.py:517-518``): the number of dependent exchange points of one launch.
+* ``install(model)`` rebinds ``model._expert_actions`` exactly like ``src/mk_expert.py:521-536``.
+
+Preconditions the reference asserts (``src/mk_expert.py:444,462,464,480,488,496``) raise
+``ValueError`` here; a failed CUDA call or a device-side wait that ran out raises ``MkxError``.
+There is no CPU path: without ``libmkx.so`` the import fails.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _lib
+from .synthetic import ExpertWeights, weights_from_model
+
+AO = 8     # real action dims the loop carries (src/mk_expert.py:478)
+TP = 16    # action rows per launch
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+class ExpertMegakernel:
+    """Packs the expert weights once; ``run`` integrates Euler steps 2..N in one launch."""
+
+    def __init__(self, model=None, *, weights: ExpertWeights | None = None, max_rows: int = TP, grid: int = 0,
+                 device=None):
+        w = weights if weights is not None else weights_from_model(model)
+        d = w.dims
+        self.L, self.NH, self.HD, self.H, self.I, self.A = d.L, d.NH, d.HD, d.H, d.I, d.A
+        self.TP = TP
+        self.eps, self.qk_eps = float(w.eps), float(w.qk_eps)
+        dev = torch.device(device) if device is not None else w.wqkv.device
+        if dev.type != "cuda":
+            raise ValueError("ExpertMegakernel needs the expert weights on a CUDA device")
+        self.device = dev
+        lib = _lib.load()
+        self._lib = lib
+        t = {k: v.to(dev).contiguous() for k, v in w.tensors().items()}
+        for k in ("wqkv", "wo", "wqca", "woca", "wg", "wu", "wd", "qn", "kn", "qcan"):
+            if t[k].dtype != torch.bfloat16:
+                raise ValueError(f"{k} must be bf16")
+        for k in ("win", "bin", "wout", "bout"):
+            t[k] = t[k].float().contiguous()
+        dims = _lib.Dims(L=d.L, H=d.H, NH=d.NH, HD=d.HD, I=d.I, A=d.A, eps=self.eps, qk_eps=self.qk_eps,
+                         max_rows=max_rows, grid=grid)
+        wts = _lib.Weights(**{f[0]: t[f[0]].data_ptr() for f in _lib.Weights._fields_})
+        handle = C.c_void_p()
+        with torch.cuda.device(dev):
+            torch.cuda.synchronize(dev)  # the packing kernels read the weights on another stream
+            _lib.check(lib.mkx_create(C.byref(dims), C.byref(wts), dev.index or 0, C.byref(handle)), "mkx_create")
+        self._h = handle
+        del t
+        g, smem = C.c_int(), C.c_int()
+        _lib.check(lib.mkx_launch_shape(self._h, C.byref(g), C.byref(smem)), "mkx_launch_shape")
+        self.nprog = g.value
+        self.cfg = dict(grid=g.value, threads=256, smem_bytes=smem.value, max_rows=max_rows, AO=AO)
+        self._dt_cache: dict = {}
+
+    # ------------------------------------------------------------------------------------------
+    def _dt_tensor(self, dt) -> torch.Tensor:
+        if isinstance(dt, torch.Tensor):
+            if dt.device != self.device:
+                raise ValueError("dt must be on the expert's device")
+            return dt.reshape(-1)[:1].float() if dt.dtype != torch.float32 else dt.reshape(-1)
+        key = float(dt)
+        if key not in self._dt_cache:
+            self._dt_cache[key] = torch.tensor([key], dtype=torch.float32, device=self.device)
+        return self._dt_cache[key]
+
+    def run(self, x_t: torch.Tensor, mods: torch.Tensor, dt, past, action_dim: int,
+            trace: torch.Tensor | None = None) -> torch.Tensor:
+        """x_t: [1, T, A] fp32 after Euler step 1; mods: [N, MODW] (row 0 = step 1, used already);
+        returns x_t after step N (padded dims as the reference: 0 + dt * v)."""
+        step = past.register_step
+        if x_t.dim() != 3 or x_t.shape[0] != 1 or x_t.shape[2] != self.A:
+            raise ValueError(f"x_t must be [1, T, {self.A}], got {tuple(x_t.shape)}")
+        T = x_t.shape[1]
+        if not (1 <= T <= self.cfg["max_rows"]) or not (1 <= action_dim <= AO):
+            raise ValueError(f"T={T} must be in 1..{self.cfg['max_rows']} and action_dim={action_dim} in 1..{AO}")
+        if mods.dim() != 2 or mods.shape[1] != 9 * self.L * self.H + 2 * self.H or mods.shape[0] < 2:
+            raise ValueError(f"mods must be [N >= 2, {9 * self.L * self.H + 2 * self.H}], got {tuple(mods.shape)}")
+        n_steps = mods.shape[0] - 1
+        mem = step["mem_kv"]
+        ca = past.cross_attn_kv
+        if len(mem) != self.L or len(ca) != self.L:
+            raise ValueError("need one memory and one cross-attention K/V pair per layer")
+
+        def kv_rows(t: torch.Tensor):
+            if t.dim() == 4 and t.shape[0] == 1:
+                t = t[0]
+            if t.dim() != 3 or t.shape[1] != self.NH or t.shape[2] != self.HD or t.dtype != torch.bfloat16:
+                raise ValueError(f"K/V must be bf16 [rows, {self.NH}, {self.HD}], got {t.dtype} {tuple(t.shape)}")
+            if t.stride(2) != 1 or t.stride(1) != self.HD:
+                raise ValueError("K/V heads must be contiguous")
+            if t.device != self.device:
+                raise ValueError("K/V must be on the expert's device")
+            return t
+        memk = [kv_rows(m[0]) for m in mem]
+        memv = [kv_rows(m[1]) for m in mem]
+        kca = [kv_rows(k[0]) for k in ca]
+        vca = [kv_rows(k[1]) for k in ca]
+        PM = memk[0].shape[0]
+        mstride = memk[0].stride(0)
+        cstride = kca[0].stride(0)
+        if any(m.shape[0] != PM or m.stride(0) != mstride for m in memk + memv):
+            raise ValueError("memory K/V of all layers must share rows and row stride")
+        if any(k.stride(0) != cstride for k in kca + vca):
+            raise ValueError("cross-attention K/V of all layers must share the row stride")
+
+        def pe(t: torch.Tensor):
+            t = t.reshape(-1, self.HD)
+            if t.shape[0] != T:
+                raise ValueError(f"RoPE tables must be [T={T}, {self.HD}], got {tuple(t.shape)}")
+            return t.float().contiguous() if t.dtype != torch.float32 else t.contiguous()
+        sa_cos, sa_sin = (pe(t) for t in step["sa_pe"])
+        ca_cos, ca_sin = (pe(t) for t in step["ca_pe"])
+        cu_kv = step["cu_kv"].to(torch.int32) if step["cu_kv"].dtype != torch.int32 else step["cu_kv"]
+        cu_src = step["cu_src"].to(torch.int32) if step["cu_src"].dtype != torch.int32 else step["cu_src"]
+        x_in = x_t.reshape(T, self.A)
+        x_in = x_in.float().contiguous() if x_in.dtype != torch.float32 else x_in.contiguous()
+        if mods.dtype not in (torch.bfloat16, torch.float32):
+            mods = mods.float()
+        mods = mods.contiguous()
+        dt_t = self._dt_tensor(dt)
+        out = torch.empty(T, self.A, dtype=torch.float32, device=self.device)
+        if trace is not None:
+            if trace.dtype != torch.bfloat16 or trace.numel() != n_steps * self.L * T * self.H or not trace.is_contiguous():
+                raise ValueError("trace must be a contiguous bf16 tensor of n_steps * L * T * H elements")
+        si = _lib.StepInputs()
+        si.x_in, si.x_out, si.mods = x_in.data_ptr(), out.data_ptr(), mods.data_ptr()
+        si.mods_fp32 = 1 if mods.dtype == torch.float32 else 0
+        si.dt = dt_t.data_ptr()
+        for l in range(self.L):
+            si.memk[l], si.memv[l] = memk[l].data_ptr(), memv[l].data_ptr()
+            si.kca[l], si.vca[l] = kca[l].data_ptr(), vca[l].data_ptr()
+        si.mem_rows, si.mem_row_stride, si.ca_row_stride = PM, mstride, cstride
+        si.ca_rows = min(k.shape[0] for k in kca + vca)
+        si.cu_kv, si.cu_src = cu_kv.data_ptr(), cu_src.data_ptr()
+        si.sa_cos, si.sa_sin, si.ca_cos, si.ca_sin = (t.data_ptr() for t in (sa_cos, sa_sin, ca_cos, ca_sin))
+        si.T, si.n_steps, si.action_dim = T, n_steps, int(action_dim)
+        si.trace_h = trace.data_ptr() if trace is not None else None
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        _lib.check(self._lib.mkx_run(self._h, C.byref(si), C.c_void_p(stream)), "mkx_run")
+        return out.reshape(1, T, self.A)
+
+    def barriers(self, n_steps: int) -> int:
+        return int(self._lib.mkx_sync_points(self._h, int(n_steps)))
+
+    # ---- status / test hooks ------------------------------------------------------------------
+    def status(self) -> tuple[int, int]:
+        """(error code, stage counter) from the device; synchronous."""
+        code, stages = C.c_int(), C.c_longlong()
+        self._lib.mkx_last_error(self._h, C.byref(code), C.byref(stages))
+        return code.value, stages.value
+
+    def check_device_error(self) -> None:
+        code, stages = C.c_int(), C.c_longlong()
+        st = self._lib.mkx_last_error(self._h, C.byref(code), C.byref(stages))
+        if st == _lib.MKX_ERR_DEVICE:
+            raise _lib.MkxError("expert_kernel", st, f"device code 0x{code.value:x} (cta << 16 | kind << 8 | stage)")
+        _lib.check(st, "mkx_last_error")
+
+    def clear_error(self) -> None:
+        _lib.check(self._lib.mkx_clear_error(self._h), "mkx_clear_error")
+
+    def set_timeout(self, seconds: float) -> None:
+        _lib.check(self._lib.mkx_set_timeout_ns(self._h, int(seconds * 1e9)), "mkx_set_timeout_ns")
+
+    def set_fault_injection(self, stage: int) -> None:
+        _lib.check(self._lib.mkx_set_fault_injection(self._h, int(stage)), "mkx_set_fault_injection")
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            self._lib.mkx_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass
+
+
+def install(model) -> ExpertMegakernel:
+    """Route ``RekiFlowModel._expert_actions`` (what ``ExpertGraphs`` captures) through the megakernel
+    for steps 2..N; modulations, register_prepare and step 1 stay the model's own callables
+    (``src/mk_expert.py:521-536``)."""
+    mk = ExpertMegakernel(model)
+    model._mk = mk
+
+    def _expert_actions(noise, cross_attn_cache, register_cache, state_cond, action_dim, num_steps):
+        if noise.shape[0] != 1:
+            raise ValueError("the megakernel path runs batch 1")
+        mods, dt = model._step_modulations(num_steps, state_cond)
+        x_t, cur_k, cur_v = model._expert_first_step(noise, cross_attn_cache, register_cache, mods[:1], dt, action_dim)
+        if num_steps > 1:
+            x_t = mk.run(x_t, mods, dt, cross_attn_cache, action_dim)
+        return x_t, cur_k, cur_v
+
+    model._expert_actions = _expert_actions
+    return mk

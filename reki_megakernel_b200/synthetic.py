@@ -1,0 +1,327 @@
+"""Seeded synthetic expert weights and Euler-loop inputs (no checkpoint or dataset exists here).
+
+Every tensor is drawn on the CPU from ``torch.Generator`` streams with fixed seeds, in a fixed order,
+so the same call gives bit-identical tensors on any machine with this torch build; callers move the
+result to the device. Shapes follow the expert the megakernel reads
+(``src/mk_expert.py:436-481`` of the reference: stacked ``[L, N, K]`` bf16 weights, fp32 action
+projections with ``win`` stored transposed ``[A, H]``) and the inputs ``ExpertMegakernel.run`` takes
+(``src/mk_expert.py:483-515``: ``x_t [1, T, A]`` fp32 after Euler step 1, ``mods [N, MODW]``, ``dt``,
+register-memory K/V ``[L, PM, NH, HD]`` valid from row ``cu_kv[0]``, cross-attention K/V
+``[L, SP, NH, HD]`` valid for ``cu_src[1]`` rows, RoPE cos/sin ``[T, HD]``).
+
+Distributions (the benchmark's synthetic workload): weights N(0, 0.02) from seed 0 (norm weights too;
+they are stored as offsets, the kernels scale by ``1 + w``); memory K/V N(0, 1); the cross-attention
+source ``[S, 2048]`` N(0, 1) x 0.5 projected to K/V by the restated ``register_prepare``; proprio
+state U(-1, 1); flow noise N(0, 1) from seed ``1234 + call`` (``src/harness.py:53-66``); dt = 0.1.
+
+The modulation network, step 1 and ``register_prepare`` belong to Kyutai's model, which is not in
+the reference; ``step_modulations`` and ``register_prepare_cpu`` below are restatements with the
+published shapes (MODW = 3L*3H + 2H; 31 M cross-attention projection weights) and are not pinned.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from types import SimpleNamespace
+
+import torch
+
+__all__ = ["ExpertDims", "ExpertWeights", "StepInputs", "make_weights", "make_inputs", "make_model",
+           "make_past", "weights_from_model", "rope_cos_sin", "step_modulations"]
+
+
+@dataclass(frozen=True)
+class ExpertDims:
+    """Expert geometry. Defaults are REKI's action expert (10 layers, width 768, 12 heads x 64,
+    MLP 3072, 32 padded action dims)."""
+    L: int = 10
+    H: int = 768
+    NH: int = 12
+    HD: int = 64
+    I: int = 3072
+    A: int = 32
+    src_dim: int = 2048
+
+    @property
+    def MODW(self) -> int:
+        return 3 * self.L * 3 * self.H + 2 * self.H
+
+    def __post_init__(self):
+        assert self.NH * self.HD == self.H, "H must equal NH * HD"
+
+
+@dataclass
+class ExpertWeights:
+    """Packed expert weights in the reference's stacked layout (``src/mk_expert.py:445-460``)."""
+    dims: ExpertDims
+    wqkv: torch.Tensor   # [L, 3H, H] bf16 = cat(q, k, v)
+    wo: torch.Tensor     # [L, H, H]
+    wqca: torch.Tensor   # [L, H, H]
+    woca: torch.Tensor   # [L, H, H]
+    wg: torch.Tensor     # [L, I, H]
+    wu: torch.Tensor     # [L, I, H]
+    wd: torch.Tensor     # [L, H, I]
+    qn: torch.Tensor     # [L, HD] (offset: scale = 1 + w)
+    kn: torch.Tensor     # [L, HD]
+    qcan: torch.Tensor   # [L, HD]
+    win: torch.Tensor    # [A, H] fp32 (action_in_proj.weight transposed)
+    bin: torch.Tensor    # [H] fp32
+    wout: torch.Tensor   # [A, H] fp32
+    bout: torch.Tensor   # [A] fp32
+    eps: float = 1e-6
+    qk_eps: float = 1e-6
+
+    def to(self, device) -> "ExpertWeights":
+        kw = {k: (v.to(device) if isinstance(v, torch.Tensor) else v) for k, v in self.__dict__.items()}
+        return ExpertWeights(**kw)
+
+    def tensors(self) -> dict:
+        return {k: v for k, v in self.__dict__.items() if isinstance(v, torch.Tensor)}
+
+
+@dataclass
+class StepInputs:
+    """Inputs of Euler steps 2..N for B episodes (B = 1 is the reference's case)."""
+    x: torch.Tensor          # [B, T, A] fp32, state after step 1
+    mods: torch.Tensor       # [B, N, MODW] bf16 (row 0 = step 1, already used)
+    dt: torch.Tensor         # [B] fp32
+    memk: torch.Tensor       # [B, L, PM, NH, HD] bf16, rows >= kv_start valid
+    memv: torch.Tensor
+    kv_start: torch.Tensor   # [B] int32
+    kca: torch.Tensor        # [B, L, SP, NH, HD] bf16, rows < S valid
+    vca: torch.Tensor
+    S: torch.Tensor          # [B] int32
+    sa_cos: torch.Tensor     # [B, T, HD] fp32
+    sa_sin: torch.Tensor
+    ca_cos: torch.Tensor
+    ca_sin: torch.Tensor
+    action_dim: int = 7
+    extra: dict = field(default_factory=dict)
+
+    @property
+    def n_steps(self) -> int:
+        return self.mods.shape[1] - 1
+
+    def to(self, device) -> "StepInputs":
+        kw = {k: (v.to(device) if isinstance(v, torch.Tensor) else v) for k, v in self.__dict__.items()}
+        return StepInputs(**kw)
+
+    def episode(self, b: int) -> "StepInputs":
+        kw = {}
+        for k, v in self.__dict__.items():
+            kw[k] = v[b:b + 1] if isinstance(v, torch.Tensor) else v
+        return StepInputs(**kw)
+
+
+def _randn(gen, shape, std, dtype=torch.bfloat16):
+    return (torch.randn(shape, generator=gen, dtype=torch.float32) * std).to(dtype)
+
+
+def make_weights(dims: ExpertDims = ExpertDims(), seed: int = 0, std: float = 0.02) -> ExpertWeights:
+    """Random-init expert weights N(0, std) on the CPU, one generator, fixed draw order."""
+    d = dims
+    g = torch.Generator().manual_seed(seed)
+    L, H, I, HD, A = d.L, d.H, d.I, d.HD, d.A
+    w = dict(
+        wqkv=_randn(g, (L, 3 * H, H), std), wo=_randn(g, (L, H, H), std),
+        wqca=_randn(g, (L, H, H), std), woca=_randn(g, (L, H, H), std),
+        wg=_randn(g, (L, I, H), std), wu=_randn(g, (L, I, H), std), wd=_randn(g, (L, H, I), std),
+        qn=_randn(g, (L, HD), std), kn=_randn(g, (L, HD), std), qcan=_randn(g, (L, HD), std),
+        win=_randn(g, (A, H), std, torch.float32), bin=_randn(g, (H,), std, torch.float32),
+        wout=_randn(g, (A, H), std, torch.float32), bout=_randn(g, (A,), std, torch.float32),
+    )
+    return ExpertWeights(dims=d, **w)
+
+
+def rope_cos_sin(positions: torch.Tensor, HD: int, theta: float = 10000.0):
+    """rotate_half RoPE tables [T, HD] (fp32): angle(t, d) = pos_t * theta^(-2 (d mod HD/2) / HD)."""
+    half = HD // 2
+    inv = theta ** (-torch.arange(half, dtype=torch.float64) * 2.0 / HD)
+    ang = positions.double()[:, None] * inv[None, :]
+    ang = torch.cat([ang, ang], dim=1)
+    return ang.cos().float(), ang.sin().float()
+
+
+def _timestep_embedding(t: torch.Tensor, dim: int = 256) -> torch.Tensor:
+    half = dim // 2
+    freqs = torch.exp(-math.log(10000.0) * torch.arange(half, dtype=torch.float32) / half)
+    a = t.float()[:, None] * 1000.0 * freqs[None, :]
+    return torch.cat([a.cos(), a.sin()], dim=1)
+
+
+def step_modulations(dims: ExpertDims, num_steps: int, state: torch.Tensor, seed: int = 0):
+    """Restated (unpinned) per-step modulation network: timestep embedding of t_s = 1 - s/N plus a
+    linear embedding of the proprio state, SiLU, then one Linear to MODW = 3L*3H + 2H values per step
+    ([scale, shift, gate] for SA, CA and MLP of each layer, then [scale, shift] of the final norm).
+    Returns (mods [N, MODW] bf16, dt scalar fp32 = 1/N)."""
+    g = torch.Generator().manual_seed(seed + 7)
+    H = dims.H
+    w_t = torch.randn((H, 256), generator=g) * 0.02
+    w_s = torch.randn((H, state.numel()), generator=g) * 0.02
+    w_m = torch.randn((dims.MODW, H), generator=g) * 0.02
+    b_m = torch.randn((dims.MODW,), generator=g) * 0.02
+    t = 1.0 - torch.arange(num_steps, dtype=torch.float32) / num_steps
+    e = _timestep_embedding(t) @ w_t.T + (state.float().reshape(1, -1) @ w_s.T)
+    e = e * 8.0  # unit-scale conditioning
+    mods = torch.nn.functional.silu(e) @ w_m.T + b_m
+    return mods.to(torch.bfloat16), torch.tensor(1.0 / num_steps, dtype=torch.float32)
+
+
+def _rms(x, eps):
+    return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps)
+
+
+def register_prepare_cpu(dims: ExpertDims, src: torch.Tensor, seed: int = 0, SP: int | None = None,
+                         eps: float = 1e-6):
+    """Restated (unpinned) cross-attention K/V preparation: per layer K = RoPE(RMSNorm_HD(src Wk^T)
+    (1 + kn)) and V = src Wv^T from the [S, src_dim] VLM source (Wk, Wv: L x 2 x [H, src_dim] =
+    31.5 M weights at REKI's sizes). Returns bf16 [L, SP, NH, HD] K and V (rows >= S zero)."""
+    L, H, NH, HD = dims.L, dims.H, dims.NH, dims.HD
+    S = src.shape[0]
+    SP = SP or S
+    g = torch.Generator().manual_seed(seed + 11)
+    k_out = torch.zeros(L, SP, NH, HD, dtype=torch.bfloat16)
+    v_out = torch.zeros(L, SP, NH, HD, dtype=torch.bfloat16)
+    cos, sin = rope_cos_sin(torch.arange(S), HD)
+    for l in range(L):
+        wk = torch.randn((H, src.shape[1]), generator=g) * 0.02
+        wv = torch.randn((H, src.shape[1]), generator=g) * 0.02
+        kn = torch.randn((HD,), generator=g) * 0.02
+        k = (src.float() @ wk.T).reshape(S, NH, HD)
+        v = (src.float() @ wv.T).reshape(S, NH, HD)
+        k = _rms(k, eps) * (1.0 + kn)
+        k1, k2 = k[..., :HD // 2], k[..., HD // 2:]
+        rot = torch.cat([-k2, k1], dim=-1)
+        k = k * cos[:, None, :] + rot * sin[:, None, :]
+        k_out[l, :S] = k.to(torch.bfloat16)
+        v_out[l, :S] = v.to(torch.bfloat16)
+    return k_out, v_out
+
+
+def make_inputs(dims: ExpertDims = ExpertDims(), *, B: int = 1, T: int = 10, n_steps: int = 9,
+                frame_slots: int = 3, frames_valid: int = 2, regs_per_frame: int = 32, S: int = 160,
+                SP: int | None = None, action_dim: int = 7, dt: float = 0.1, seed: int = 0,
+                noise_seed: int = 1234, poison: bool = False) -> StepInputs:
+    """Seeded inputs of Euler steps 2..N for B episodes (episode b uses seeds offset by b).
+
+    ``poison`` fills with NaN every value the loop must ignore: memory rows before kv_start, source
+    rows >= S and the input action dims >= action_dim, so a stray read shows in the output.
+    """
+    d = dims
+    L, NH, HD, A = d.L, d.NH, d.HD, d.A
+    PM = frame_slots * regs_per_frame
+    kv_start = (frame_slots - frames_valid) * regs_per_frame
+    SP = SP or (max(64, -(-S // 64) * 64))
+    xs, mods, memk, memv, kca, vca, sac, sas, cac, cas = ([] for _ in range(10))
+    for b in range(B):
+        g = torch.Generator().manual_seed(seed + 1000 * b + 1)
+        gn = torch.Generator().manual_seed(noise_seed + b)
+        x = torch.randn((T, A), generator=gn, dtype=torch.float32)
+        state = torch.rand((7,), generator=g) * 2.0 - 1.0
+        m, _ = step_modulations(d, n_steps + 1, state, seed=seed)
+        mk = torch.randn((L, PM, NH, HD), generator=g).to(torch.bfloat16)
+        mv = torch.randn((L, PM, NH, HD), generator=g).to(torch.bfloat16)
+        src = torch.randn((S, d.src_dim), generator=g) * 0.5
+        k, v = register_prepare_cpu(d, src, seed=seed, SP=SP)
+        if poison:
+            x[:, action_dim:] = float("nan")  # the loop zero-pads these dims (src/mk_expert.py:285)
+            mk[:, :kv_start] = float("nan")
+            mv[:, :kv_start] = float("nan")
+            k[:, S:] = float("nan")
+            v[:, S:] = float("nan")
+        c1, s1 = rope_cos_sin(torch.arange(T) + PM, HD)
+        c2, s2 = rope_cos_sin(torch.arange(T), HD)
+        xs.append(x); mods.append(m); memk.append(mk); memv.append(mv); kca.append(k); vca.append(v)
+        sac.append(c1); sas.append(s1); cac.append(c2); cas.append(s2)
+    st = lambda t: torch.stack(t).contiguous()  # noqa: E731
+    return StepInputs(
+        x=st(xs), mods=st(mods), dt=torch.full((B,), dt, dtype=torch.float32),
+        memk=st(memk), memv=st(memv), kv_start=torch.full((B,), kv_start, dtype=torch.int32),
+        kca=st(kca), vca=st(vca), S=torch.full((B,), S, dtype=torch.int32),
+        sa_cos=st(sac), sa_sin=st(sas), ca_cos=st(cac), ca_sin=st(cas), action_dim=action_dim)
+
+
+def make_past(inp: StepInputs, b: int = 0):
+    """The ``past`` object ``ExpertMegakernel.run`` reads (``src/mk_expert.py:486-495``) for episode b:
+    ``register_step`` with ``mem_kv`` (per-layer (K, V) [PM, NH, HD]), ``sa_pe``/``ca_pe`` (cos, sin),
+    ``cu_kv`` = [kv_start, PM], ``cu_src`` = [0, S]; ``cross_attn_kv`` per-layer (K, V) [SP, NH, HD]."""
+    L = inp.memk.shape[1]
+    dev = inp.memk.device
+    step = {
+        "mem_kv": [(inp.memk[b, l], inp.memv[b, l]) for l in range(L)],
+        "sa_pe": (inp.sa_cos[b], inp.sa_sin[b]),
+        "ca_pe": (inp.ca_cos[b], inp.ca_sin[b]),
+        "cu_kv": torch.stack([inp.kv_start[b], torch.tensor(inp.memk.shape[2], dtype=torch.int32, device=dev)]),
+        "cu_src": torch.stack([torch.tensor(0, dtype=torch.int32, device=dev), inp.S[b]]),
+    }
+    return SimpleNamespace(register_step=step, cross_attn_kv=[(inp.kca[b, l], inp.vca[b, l]) for l in range(L)])
+
+
+def _lin(w: torch.Tensor, b: torch.Tensor | None = None):
+    return SimpleNamespace(weight=w, bias=b, in_features=w.shape[1], out_features=w.shape[0])
+
+
+def make_model(w: ExpertWeights):
+    """A duck-typed model exposing exactly the attributes the reference's ``ExpertMegakernel``
+    reads (``src/mk_expert.py:437-464``): ``vlm_with_expert.action_expert.layers[i]`` with
+    ``self_attn.{q,k,v,o}_proj/q_norm/k_norm``, ``cross_attn.{q_proj,o_proj,q_norm}``,
+    ``mlp.{gate,up,down}_proj/act_fn``, ``input_layernorm.eps``; ``action_expert.norm.eps``;
+    ``action_in_proj`` and ``action_out_proj``."""
+    d = w.dims
+    H = d.H
+    layers = []
+    for l in range(d.L):
+        sa = SimpleNamespace(
+            q_proj=_lin(w.wqkv[l, :H]), k_proj=_lin(w.wqkv[l, H:2 * H]), v_proj=_lin(w.wqkv[l, 2 * H:]),
+            o_proj=_lin(w.wo[l]), q_norm=SimpleNamespace(weight=w.qn[l], eps=w.qk_eps),
+            k_norm=SimpleNamespace(weight=w.kn[l], eps=w.qk_eps), n_q_heads=d.NH, n_kv_heads=d.NH,
+            head_dim=d.HD)
+        ca = SimpleNamespace(q_proj=_lin(w.wqca[l]), o_proj=_lin(w.woca[l]),
+                             q_norm=SimpleNamespace(weight=w.qcan[l], eps=w.qk_eps), n_kv_heads=d.NH)
+        mlp = SimpleNamespace(gate_proj=_lin(w.wg[l]), up_proj=_lin(w.wu[l]), down_proj=_lin(w.wd[l]),
+                              act_fn=torch.nn.SiLU())
+        layers.append(SimpleNamespace(self_attn=sa, cross_attn=ca, mlp=mlp,
+                                      input_layernorm=SimpleNamespace(eps=w.eps)))
+    expert = SimpleNamespace(layers=layers, norm=SimpleNamespace(eps=w.eps))
+    return SimpleNamespace(
+        vlm_with_expert=SimpleNamespace(action_expert=expert),
+        action_in_proj=_lin(w.win.t().contiguous(), w.bin),     # Linear(A -> H): weight [H, A]
+        action_out_proj=_lin(w.wout, w.bout))                    # Linear(H -> A): weight [A, H]
+
+
+def weights_from_model(model) -> ExpertWeights:
+    """Stack a model's expert weights the way ``ExpertMegakernel.__init__`` does
+    (``src/mk_expert.py:437-463``), validating the same preconditions."""
+    vwe = model.vlm_with_expert
+    layers = list(vwe.action_expert.layers)
+    sa0 = layers[0].self_attn
+    L, NH, HD = len(layers), sa0.n_q_heads, sa0.head_dim
+    H = NH * HD
+    I = layers[0].mlp.gate_proj.out_features
+    A = model.action_in_proj.in_features
+    if sa0.n_kv_heads != NH or layers[0].cross_attn.n_kv_heads != NH:
+        raise ValueError("expert attention must have n_kv_heads == n_q_heads")
+    if type(layers[0].mlp.act_fn).__name__ not in ("SiLU", "SiLUActivation"):
+        raise ValueError("expert MLP activation must be SiLU")
+    eps = float(layers[0].input_layernorm.eps)
+    if float(vwe.action_expert.norm.eps) != eps:
+        raise ValueError("final norm eps differs from the layer norm eps")
+
+    def st(f):
+        return torch.stack([f(m).detach() for m in layers]).contiguous()
+    dims = ExpertDims(L=L, H=H, NH=NH, HD=HD, I=I, A=A)
+    bf = torch.bfloat16
+    return ExpertWeights(
+        dims=dims,
+        wqkv=st(lambda m: torch.cat([m.self_attn.q_proj.weight, m.self_attn.k_proj.weight,
+                                     m.self_attn.v_proj.weight], 0)).to(bf),
+        wo=st(lambda m: m.self_attn.o_proj.weight).to(bf), wqca=st(lambda m: m.cross_attn.q_proj.weight).to(bf),
+        woca=st(lambda m: m.cross_attn.o_proj.weight).to(bf), wg=st(lambda m: m.mlp.gate_proj.weight).to(bf),
+        wu=st(lambda m: m.mlp.up_proj.weight).to(bf), wd=st(lambda m: m.mlp.down_proj.weight).to(bf),
+        qn=st(lambda m: m.self_attn.q_norm.weight).to(bf), kn=st(lambda m: m.self_attn.k_norm.weight).to(bf),
+        qcan=st(lambda m: m.cross_attn.q_norm.weight).to(bf),
+        win=model.action_in_proj.weight.detach().float().t().contiguous(),
+        bin=model.action_in_proj.bias.detach().float().contiguous(),
+        wout=model.action_out_proj.weight.detach().float().contiguous(),
+        bout=model.action_out_proj.bias.detach().float().contiguous(),
+        eps=eps, qk_eps=float(sa0.q_norm.eps))

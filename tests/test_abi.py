@@ -1,0 +1,82 @@
+"""The C ABI without a GPU: the library loads, exports every entry point ``include/mkx.h``
+declares, its structs have the same layout in C and in the ctypes binding, and argument checks
+that need no device reject bad calls."""
+import ctypes as C
+import re
+import shutil
+import subprocess
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = ROOT / "include" / "mkx.h"
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(mkx_[a-z_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    from reki_megakernel_b200 import _lib
+    lib = _lib.load()
+    syms = declared_symbols()
+    assert len(syms) >= 10
+    for s in syms:
+        assert hasattr(lib, s), s
+    assert set(syms) == set(_lib.SIGNATURES), set(syms) ^ set(_lib.SIGNATURES)
+    nm = shutil.which("nm")
+    if nm:
+        out = subprocess.run([nm, "-D", "--defined-only", str(_lib.lib_path())], capture_output=True, text=True).stdout
+        exported = set(re.findall(r"\b(mkx_[a-z_]+)\b", out))
+        assert set(syms) <= exported
+
+
+def _c_layout(struct: str, fields):
+    gcc = shutil.which("gcc")
+    if not gcc:
+        pytest.skip("gcc missing")
+    body = "".join(f'printf("{f} %zu\\n", offsetof({struct}, {f}));' for f in fields)
+    src = f'#include <stdio.h>\n#include <stddef.h>\n#include "mkx.h"\nint main(void){{{body} printf("sizeof %zu\\n", sizeof({struct})); return 0;}}\n'
+    import tempfile
+    from pathlib import Path
+    with tempfile.TemporaryDirectory() as d:
+        c = Path(d) / "l.c"
+        c.write_text(src)
+        exe = Path(d) / "l"
+        r = subprocess.run([gcc, "-I", str(ROOT / "include"), "-I", "/usr/local/cuda/include", str(c), "-o", str(exe)],
+                           capture_output=True, text=True)
+        assert r.returncode == 0, r.stderr
+        out = subprocess.run([str(exe)], capture_output=True, text=True).stdout
+    return {k: int(v) for k, v in (line.split() for line in out.splitlines())}
+
+
+@pytest.mark.parametrize("struct,cls", [("mkx_dims", "Dims"), ("mkx_weights", "Weights"), ("mkx_step_inputs", "StepInputs")])
+def test_struct_layout_matches_c(struct, cls):
+    from reki_megakernel_b200 import _lib
+    ct = getattr(_lib, cls)
+    fields = [f[0] for f in ct._fields_]
+    c = _c_layout(struct, fields)
+    for f in fields:
+        assert getattr(ct, f).offset == c[f], (struct, f, getattr(ct, f).offset, c[f])
+    assert C.sizeof(ct) == c["sizeof"]
+
+
+def test_null_arguments_are_rejected_without_a_device():
+    from reki_megakernel_b200 import _lib
+    lib = _lib.load()
+    h = C.c_void_p()
+    assert lib.mkx_create(None, None, 0, C.byref(h)) == _lib.MKX_ERR_INVALID_ARG
+    assert lib.mkx_run(None, None, None) == _lib.MKX_ERR_INVALID_ARG
+    assert lib.mkx_sync_points(None, 9) == -1
+    assert lib.mkx_set_timeout_ns(None, 1) == _lib.MKX_ERR_INVALID_ARG
+    assert lib.mkx_set_fault_injection(None, 1) == _lib.MKX_ERR_INVALID_ARG
+    assert lib.mkx_clear_error(None) == _lib.MKX_ERR_INVALID_ARG
+    assert lib.mkx_last_error(None, None, None) == _lib.MKX_ERR_INVALID_ARG
+    assert lib.mkx_launch_shape(None, None, None) == _lib.MKX_ERR_INVALID_ARG
+    d = _lib.Dims(L=10, H=1024, NH=16, HD=64, I=3072, A=32, eps=1e-6, qk_eps=1e-6, max_rows=16, grid=0)
+    w = _lib.Weights(*([1] * 14))
+    assert lib.mkx_create(C.byref(d), C.byref(w), 0, C.byref(h)) == _lib.MKX_ERR_UNSUPPORTED
+    lib.mkx_destroy(None)
