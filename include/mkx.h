@@ -99,6 +99,8 @@ typedef struct {
   int n_steps;            /* Euler steps to run (= N - 1), >= 1 */
   int action_dim;         /* real action dims, 1..8 */
   uint16_t* trace_h;      /* optional [n_steps, L, T, H] bf16: every layer's output h; may be NULL */
+  unsigned long long* prof; /* optional [grid, 1 + mkx_sync_points(n_steps)] %globaltimer stamps (ns):
+                             * per CTA, the launch start then the end of every stage; may be NULL */
 } mkx_step_inputs;
 
 /* Packs the weights into the handle's own device memory (one-off, synchronous on `stream`'s

@@ -37,7 +37,7 @@ class StepInputs(C.Structure):
                 ("kca", P * MAX_LAYERS), ("vca", P * MAX_LAYERS), ("ca_rows", C.c_int), ("ca_row_stride", C.c_int),
                 ("cu_src", P),
                 ("sa_cos", P), ("sa_sin", P), ("ca_cos", P), ("ca_sin", P),
-                ("T", C.c_int), ("n_steps", C.c_int), ("action_dim", C.c_int), ("trace_h", P)]
+                ("T", C.c_int), ("n_steps", C.c_int), ("action_dim", C.c_int), ("trace_h", P), ("prof", P)]
 
 
 SIGNATURES = {

@@ -10,6 +10,8 @@
 //   per stage, a whole layer ahead, completion on an mbarrier. Six single-buffered slots (QKV, O,
 //   CA-Q, CA-O, gate+up, down) hold one layer; a slot is refilled for the next layer as soon as
 //   its MMA has read it.
+// * Modulation vectors ([scale, shift, gate] per sub-block, [scale, shift] of the final norm) are
+//   streamed by TMA into a two-slot shared-memory ring two blocks ahead of their use.
 // * Stage-to-stage exchange: activations go through small L2-resident buffers of 8-byte words
 //   {bf16 x2 payload, 32-bit tag}. A consumer polls the words it needs until every tag equals the
 //   producing stage's epoch: the poll is the data load, so no separate grid barrier or flag
@@ -19,10 +21,11 @@
 //   shared memory, the activations as the 8-column B operand, fp32 accumulate; K split across
 //   warps, partials reduced through shared memory; fused epilogues (bf16 rounding, gated residual,
 //   SiLU-mul).
-// * Attention: one CTA per (head, action row) unit; K/V rows prefetched into registers before the
+// * Attention: one CTA per (head, action row) unit; K/V rows loaded into registers before the
 //   query is available; fp32 softmax; bf16(P) V.
-// * Euler step tail: every CTA recomputes it (final AdaRMS, fp32 velocity of the real action dims,
-//   Euler update, fp32 in-projection) so the next step's first GEMM needs no extra exchange.
+// * Euler step tail: CTA n < T computes the fp32 velocity of action row n and publishes the new
+//   action state (one small exchange); every CTA then recomputes the fp32 in-projection locally,
+//   so the next step's first GEMM reads its input from shared memory.
 // * Every spin-wait is bounded (%globaltimer); a timeout records an error word that all CTAs
 //   watch, in-flight bulk copies are drained, and the kernel returns.
 #include <cuda_runtime.h>
@@ -40,19 +43,22 @@ namespace mkx {
 
 constexpr int H = 768, NH = 12, HD = 64;
 constexpr int NT = 256, NW = 8;          // threads / warps per CTA
+constexpr int ISSUER = NT - 1;           // thread that refills weight / modulation slots
 constexpr int TP = 16;                   // padded action rows
 constexpr int AO = 8;                    // carried action dims (src/mk_expert.py:478)
 constexpr int XS = H + 8;                // shared X row stride (bf16 elements): conflict-free B loads
 constexpr int HWORDS = H / 2;            // exchange words per H-wide row
 constexpr int QKVWORDS = 3 * H / 2;
+constexpr int XWORDS = 32;               // exchange words per action-state row (fp32 payloads)
 constexpr int MAXK = 8;                  // keys per 8-lane group per attention chunk (x32 groups)
 constexpr int RESW = 8;                  // residual columns kept per CTA (o / ca-o / down rows)
-constexpr int TAIL_FLOATS = 2 * AO * H + H + 32;   // wout rows 0..7 | win rows 0..7 | bin | bout
-constexpr int TAIL_BYTES = TAIL_FLOATS * 4;
+constexpr int TAIL_FLOATS = AO * H + H + 32;   // win rows 0..7 | bin | bout (padded)
 constexpr int MAX_STEP_TAGS = 4096;      // tag = seq * 4096 + instance + 1
 
-enum Buf { B_QKV = 0, B_Y, B_H2, B_QCA, B_YCA, B_H3, B_G, B_HOUT, NBUF };
+enum Buf { B_QKV = 0, B_Y, B_H2, B_QCA, B_YCA, B_H3, B_G, B_HOUT, B_X, NBUF };
 enum Slot { S_QKV = 0, S_O, S_QCA, S_OCA, S_GU, S_D, NSLOT };
+constexpr int BAR_MODS = NSLOT;          // mbarriers NSLOT, NSLOT + 1: modulation ring slots
+constexpr int NBAR = NSLOT + 2;
 enum Stage { ST_INIT = 0, ST_QKV, ST_SA, ST_O, ST_CAQ, ST_CA, ST_OCA, ST_GU, ST_DOWN, ST_TAIL, ST_MBAR };
 enum Kind { K_TIMEOUT = 1, K_MBAR = 3 };
 
@@ -78,13 +84,14 @@ struct Params {
   const float* ca_cos;
   const float* ca_sin;
   uint16_t* trace_h;
+  unsigned long long* prof;
   unsigned long long timeout_ns;
   int drop_stage;                 // test hook: CTA 0 withholds its layer-0 words of this stage
   int mem_rows, mem_row_stride, ca_rows, ca_row_stride;
   int L, I, T, A, adim, n_steps;
   float eps, qk_eps, sm_scale;
   int s_slot[NSLOT];              // shared-memory byte offsets
-  int s_u, s_p, s_x, s_res, s_red, s_bar, s_cnt;
+  int s_x, s_p, s_mods, s_xs, s_res, s_red, s_bar, s_cnt;
 };
 
 __host__ __device__ __forceinline__ int part_lo(int i, int P, int G) {
@@ -92,49 +99,60 @@ __host__ __device__ __forceinline__ int part_lo(int i, int P, int G) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// mods: bf16 or fp32 rows; a "pair" is two consecutive columns.
-template <typename ModT> struct ModPair;
-template <> struct ModPair<uint16_t> {
-  uint32_t v;
-  __device__ __forceinline__ void load(const uint16_t* m, int col) {
-    v = __ldg(reinterpret_cast<const unsigned int*>(m + col));
-  }
-  __device__ __forceinline__ float lo() const { return bf_lo(v); }
-  __device__ __forceinline__ float hi() const { return bf_hi(v); }
-};
-template <> struct ModPair<float> {
-  float2 v;
-  __device__ __forceinline__ void load(const float* m, int col) {
-    v = __ldg(reinterpret_cast<const float2*>(m + col));
-  }
-  __device__ __forceinline__ float lo() const { return v.x; }
-  __device__ __forceinline__ float hi() const { return v.y; }
-};
-template <typename ModT> __device__ __forceinline__ float mod_at(const ModT* m, int col);
-template <> __device__ __forceinline__ float mod_at<uint16_t>(const uint16_t* m, int col) {
-  return bf_at(__ldg(reinterpret_cast<const unsigned short*>(m + col)));
+// Modulation values held in shared memory as bf16 or fp32.
+template <typename ModT> __device__ __forceinline__ float2 mod2(const ModT* m, int col);
+template <> __device__ __forceinline__ float2 mod2<uint16_t>(const uint16_t* m, int col) {
+  const uint32_t v = *reinterpret_cast<const uint32_t*>(m + col);
+  return make_float2(bf_lo(v), bf_hi(v));
 }
-template <> __device__ __forceinline__ float mod_at<float>(const float* m, int col) { return __ldg(m + col); }
+template <> __device__ __forceinline__ float2 mod2<float>(const float* m, int col) {
+  return *reinterpret_cast<const float2*>(m + col);
+}
 
 // ---------------------------------------------------------------------------------------------
+// Dynamic shared memory of the persistent kernel; regions at the Params s_* offsets. Named at
+// namespace scope so every access compiles to 32-bit shared-window addressing.
+extern __shared__ __align__(1024) char g_smem[];
+
 struct Cta {
-  char* slot[NSLOT];
-  char* U;         // union: X [TP][XS] bf16 during GEMM stages, tail weights during the step tail
-  float* P;        // partials [NW][16][16] / attention reductions [32][64]
-  float* xs;       // action state [TP][32]
-  float* res;      // residual columns [TP][RESW]
-  float* red;      // small reductions
-  uint64_t* bar;   // NSLOT weight slots + 1 tail region
-  int* cnt;        // issued[NSLOT + 1], consumed[NSLOT + 1]
   int r0_qkv, R_qkv, c0, R_h, u0, R_gu;
-  uint32_t slot_bytes[NSLOT];
   uint32_t tag0;
   int tid, warp, lane, cta, G;
   int stages;
 };
+// Shared-memory regions (offsets live in the kernel parameters, so nothing stays in registers).
+__device__ __forceinline__ char* cSlot(const Params& p, const Cta& c, int s) { return g_smem + p.s_slot[s]; }
+__device__ __forceinline__ char* cX(const Params& p, const Cta& c) { return g_smem + p.s_x; }       // [TP][XS] bf16
+__device__ __forceinline__ float* cP(const Params& p, const Cta& c) {                          // partials / attention
+  return reinterpret_cast<float*>(g_smem + p.s_p);
+}
+__device__ __forceinline__ char* cMods(const Params& p, const Cta& c) { return g_smem + p.s_mods; }  // 2 x 3H ModT
+__device__ __forceinline__ float* cXs(const Params& p, const Cta& c) {                         // action state [TP][32]
+  return reinterpret_cast<float*>(g_smem + p.s_xs);
+}
+__device__ __forceinline__ float* cRes(const Params& p, const Cta& c) {                        // residual [TP][RESW]
+  return reinterpret_cast<float*>(g_smem + p.s_res);
+}
+__device__ __forceinline__ float* cRed(const Params& p, const Cta& c) {                        // small reductions
+  return reinterpret_cast<float*>(g_smem + p.s_red);
+}
+__device__ __forceinline__ uint64_t* cBar(const Params& p, const Cta& c) {                     // NBAR mbarriers
+  return reinterpret_cast<uint64_t*>(g_smem + p.s_bar);
+}
+__device__ __forceinline__ int* cCnt(const Params& p, const Cta& c) {                          // issued, consumed
+  return reinterpret_cast<int*>(g_smem + p.s_cnt);
+}
 
 __device__ __forceinline__ void record_error(const Params& p, const Cta& c, int kind, int stage) {
   atomicCAS(p.status, 0, (c.cta << 16) | (kind << 8) | stage);
+}
+
+// Optional timeline: thread 0 of every CTA stamps %globaltimer at the launch start (index 0) and at
+// the end of every stage (index 1 + stage).
+__device__ __forceinline__ void stage_done(const Params& p, Cta& c) {
+  c.stages++;
+  if (p.prof != nullptr && c.tid == 0)
+    p.prof[(size_t)c.cta * (2 + p.n_steps * (8 * p.L + 1)) + c.stages] = globaltimer();
 }
 
 __device__ __forceinline__ const uint16_t* slot_src(const Params& p, const Cta& c, int slot, int l) {
@@ -149,26 +167,54 @@ __device__ __forceinline__ const uint16_t* slot_src(const Params& p, const Cta& 
   }
 }
 
-// Thread 0 only.
-__device__ __forceinline__ void issue_slot(const Params& p, Cta& c, int slot, int l) {
-  fence_proxy_async();
-  mbar_expect_tx(&c.bar[slot], c.slot_bytes[slot]);
-  bulk_g2s(c.slot[slot], slot_src(p, c, slot, l), c.slot_bytes[slot], &c.bar[slot]);
-  c.cnt[slot] += 1;
+// ISSUER thread only.
+__device__ __forceinline__ uint32_t slot_bytes(const Params& p, const Cta& c, int slot) {
+  switch (slot) {
+    case S_QKV: return (uint32_t)c.R_qkv * H * 2;
+    case S_GU: return (uint32_t)c.R_gu * H * 4;
+    case S_D: return (uint32_t)c.R_h * p.I * 2;
+    default: return (uint32_t)c.R_h * H * 2;
+  }
 }
-__device__ __forceinline__ void issue_tail(const Params& p, Cta& c) {
+__device__ __forceinline__ void issue_slot(const Params& p, Cta& c, int slot, int l) {
+  const uint32_t bytes = slot_bytes(p, c, slot);
   fence_proxy_async();
-  mbar_expect_tx(&c.bar[NSLOT], TAIL_BYTES);
-  bulk_g2s(c.U, p.tailw, TAIL_BYTES, &c.bar[NSLOT]);
-  c.cnt[NSLOT] += 1;
+  mbar_expect_tx(&cBar(p, c)[slot], bytes);
+  bulk_g2s(cSlot(p, c, slot), slot_src(p, c, slot, l), bytes, &cBar(p, c)[slot]);
+  cCnt(p, c)[slot] += 1;
+}
+
+// Modulation blocks: per Euler step s, 3L + 1 blocks in use order: for each layer l the SA, CA and
+// MLP blocks [scale, shift, gate] (3H values at 9Hl + 3Hb of the step's row, src/mk_expert.py:336-340),
+// then the final-norm block [scale, shift] (2H values at 9HL, src/mk_expert.py:423). Block q goes to
+// ring slot q & 1. ISSUER thread only.
+template <typename ModT>
+__device__ __forceinline__ void issue_mods(const Params& p, Cta& c, int q) {
+  const int per = 3 * p.L + 1;
+  if (q >= p.n_steps * per) return;
+  const int s = q / per, r = q % per;
+  const size_t MODW = (size_t)9 * p.L * H + 2 * H;
+  const size_t off = (size_t)(1 + s) * MODW + (r < 3 * p.L ? (size_t)9 * H * (r / 3) + (size_t)3 * H * (r % 3)
+                                                           : (size_t)9 * H * p.L);
+  const uint32_t bytes = (uint32_t)((r < 3 * p.L ? 3 : 2) * H * sizeof(ModT));
+  const int b = BAR_MODS + (q & 1);
+  fence_proxy_async();
+  mbar_expect_tx(&cBar(p, c)[b], bytes);
+  bulk_g2s(cMods(p, c) + (size_t)(q & 1) * 3 * H * sizeof(ModT), reinterpret_cast<const ModT*>(p.mods) + off, bytes,
+           &cBar(p, c)[b]);
+  cCnt(p, c)[b] += 1;
+}
+template <typename ModT>
+__device__ __forceinline__ const ModT* mods_slot(const Params& p, const Cta& c, int q) {
+  return reinterpret_cast<const ModT*>(cMods(p, c) + (size_t)(q & 1) * 3 * H * sizeof(ModT));
 }
 
 // All threads. Returns false on timeout (error recorded).
 __device__ bool wait_bar(const Params& p, Cta& c, int b) {
-  const uint32_t parity = (uint32_t)(c.cnt[NSLOT + 1 + b] & 1);
+  const uint32_t parity = (uint32_t)(cCnt(p, c)[NBAR + b] & 1);
   uint32_t spins = 0;
   uint64_t t0 = 0;
-  while (!mbar_try_wait(&c.bar[b], parity)) {
+  while (!mbar_try_wait(&cBar(p, c)[b], parity)) {
     if ((++spins & 255u) == 0u) {
       const uint64_t now = globaltimer();
       if (t0 == 0) {
@@ -182,37 +228,50 @@ __device__ bool wait_bar(const Params& p, Cta& c, int b) {
   return true;
 }
 // After every thread passed wait_bar(b) and a __syncthreads: thread 0 bumps the consumed count.
-__device__ __forceinline__ void consumed(Cta& c, int b) {
-  if (c.tid == 0) c.cnt[NSLOT + 1 + b] += 1;
+__device__ __forceinline__ void consumed(const Params& p, Cta& c, int b) {
+  if (c.tid == 0) cCnt(p, c)[NBAR + b] += 1;
 }
 
-// Poll N 16-byte pairs of exchange words until both tags of every valid pair equal `tag`.
+// Exchange polls. issue_pairs loads N 16-byte pairs of words at addr(i) (entries outside `valid`
+// count as fresh); complete_pairs re-polls the stale ones until both tags of every pair equal `tag`.
+// Addresses are recomputed rather than held, to keep registers for the data.
 // Returns 0, or the Waiter code (1 timeout, 2 abort seen).
-template <int N>
-__device__ __forceinline__ int poll_pairs(const u64* (&ptr)[N], u64 (&w0)[N], u64 (&w1)[N], uint32_t valid,
-                                          uint32_t tag, Waiter& wt) {
+template <int N, typename Addr>
+__device__ __forceinline__ void issue_pairs(Addr addr, u64 (&w0)[N], u64 (&w1)[N], uint32_t valid, uint32_t tag) {
 #pragma unroll
   for (int i = 0; i < N; ++i) {
     if ((valid >> i) & 1u) {
-      ld_volatile_v2(ptr[i], w0[i], w1[i]);
+      ld_volatile_v2(addr(i), w0[i], w1[i]);
     } else {
       w0[i] = make_word(tag, 0u);
       w1[i] = w0[i];
     }
   }
+}
+template <int N, typename Addr>
+__device__ __forceinline__ int complete_pairs(Addr addr, u64 (&w0)[N], u64 (&w1)[N], uint32_t tag, Waiter& wt) {
   while (true) {
     uint32_t bad = 0;
 #pragma unroll
     for (int i = 0; i < N; ++i) {
       if (tag_of(w0[i]) != tag || tag_of(w1[i]) != tag) {
         bad |= 1u << i;
-        ld_volatile_v2(ptr[i], w0[i], w1[i]);
+        ld_volatile_v2(addr(i), w0[i], w1[i]);
       }
     }
     if (bad == 0u) return 0;
     const int r = wt.tick();
     if (r) return r;
   }
+}
+__device__ __forceinline__ int poll_word(const u64* ptr, u64& w, uint32_t tag, Waiter& wt) {
+  w = ld_volatile(ptr);
+  while (tag_of(w) != tag) {
+    const int r = wt.tick();
+    if (r) return r;
+    w = ld_volatile(ptr);
+  }
+  return 0;
 }
 
 __device__ __forceinline__ int fail_code(const Params& p, const Cta& c, int r, int stage) {
@@ -223,75 +282,86 @@ __device__ __forceinline__ int fail_code(const Params& p, const Cta& c, int r, i
 // ---------------------------------------------------------------------------------------------
 // AdaRMS staging: thread (n = tid / 16, part = tid % 16) owns 12 word pairs of action row n,
 // q = part + 16 j, i.e. columns {16kb + 2cc, +1} and {16kb + 2cc + 8, +9} with kb = q / 4, cc = q % 4.
-// hv[2j], hv[2j+1]: the two bf16-pair payloads. Writes a = bf16(h * rstd * (1 + scale) + shift)
-// into X (rows >= T zero) and keeps h at the CTA's residual columns (src/mk_expert.py:93-122).
 __device__ __forceinline__ int col_a_of(int q) { return 16 * (q >> 2) + 2 * (q & 3); }
 
-template <typename ModT>
-__device__ int load_rows_poll(const Params& p, const Cta& c, const u64* rows, uint32_t tag, uint32_t (&hv)[24],
-                              int stage) {
+// Polls action rows (row n of thread n = tid / 16) of an exchange buffer and writes the raw bf16
+// values into X (natural layout). Returns nonzero on a failed wait (not CTA-uniform).
+__device__ int poll_rows_to_x(const Params& p, const Cta& c, const u64* rows, uint32_t tag, int stage) {
   const int n = c.tid >> 4, part = c.tid & 15;
-  const u64* ptr[12];
+  const u64* base = rows + (size_t)n * HWORDS + 2 * part;
+  auto addr = [base](int j) { return base + 32 * j; };
   u64 w0[12], w1[12];
-#pragma unroll
-  for (int j = 0; j < 12; ++j) ptr[j] = rows + (size_t)n * HWORDS + 2 * (part + 16 * j);
   Waiter wt(p.status, p.timeout_ns);
-  const int r = poll_pairs<12>(ptr, w0, w1, n < p.T ? 0xfffu : 0u, tag, wt);
+  issue_pairs<12>(addr, w0, w1, n < p.T ? 0xfffu : 0u, tag);
+  const int r = complete_pairs<12>(addr, w0, w1, tag, wt);
+  char* xrow = cX(p, c) + (size_t)n * XS * 2;
 #pragma unroll
   for (int j = 0; j < 12; ++j) {
-    hv[2 * j] = payload_of(w0[j]);
-    hv[2 * j + 1] = payload_of(w1[j]);
+    const int ca = col_a_of(part + 16 * j);
+    *reinterpret_cast<uint32_t*>(xrow + ca * 2) = payload_of(w0[j]);
+    *reinterpret_cast<uint32_t*>(xrow + (ca + 8) * 2) = payload_of(w1[j]);
   }
   return fail_code(p, c, r, stage);
 }
 
+// In place on X (raw h in, after a __syncthreads): a = bf16(h * rstd * (1 + scale) + shift), rows
+// >= T zero, and h kept at the CTA's residual columns (src/mk_expert.py:93-122). msc: [scale H |
+// shift H] in shared memory. Thread (n = tid / 16, part) owns the 48 columns of word pairs
+// part + 16 j of row n; loops are kept rolled to keep the routine small.
 template <typename ModT>
-__device__ void stage_adarms(const Params& p, Cta& c, const uint32_t (&hv)[24], const ModT* msc) {
+__device__ void stage_adarms(const Params& p, Cta& c, const ModT* msc) {
   const int n = c.tid >> 4, part = c.tid & 15;
   const ModT* msh = msc + H;
+  char* xrow = cX(p, c) + (size_t)n * XS * 2;
+  const bool live = n < p.T;
   float ss = 0.f;
-#pragma unroll
-  for (int j = 0; j < 24; ++j) {
-    const float a = bf_lo(hv[j]), b = bf_hi(hv[j]);
+#pragma unroll 2
+  for (int j = 0; j < 12; ++j) {
+    const int ca = col_a_of(part + 16 * j);
+    const uint32_t u = *reinterpret_cast<const uint32_t*>(xrow + ca * 2);
+    const uint32_t v = *reinterpret_cast<const uint32_t*>(xrow + (ca + 8) * 2);
+    const float a = bf_lo(u), b = bf_hi(u), d = bf_lo(v), e = bf_hi(v);
     ss = fmaf(a, a, ss);
     ss = fmaf(b, b, ss);
+    ss = fmaf(d, d, ss);
+    ss = fmaf(e, e, ss);
   }
   ss += __shfl_xor_sync(0xffffffffu, ss, 8);
   ss += __shfl_xor_sync(0xffffffffu, ss, 4);
   ss += __shfl_xor_sync(0xffffffffu, ss, 2);
   ss += __shfl_xor_sync(0xffffffffu, ss, 1);
   const float rstd = rsqrtf(ss / (float)H + p.eps);
-  const bool live = n < p.T;
-  char* xrow = c.U + (size_t)n * XS * 2;
-#pragma unroll
-  for (int j = 0; j < 12; ++j) {
-    const int q = part + 16 * j;
-    const int ca = col_a_of(q), cb = ca + 8;
-    ModPair<ModT> sa, sb, ha, hb;
-    sa.load(msc, ca);
-    sb.load(msc, cb);
-    ha.load(msh, ca);
-    hb.load(msh, cb);
-    const float h0 = bf_lo(hv[2 * j]), h1 = bf_hi(hv[2 * j]);
-    const float h2 = bf_lo(hv[2 * j + 1]), h3 = bf_hi(hv[2 * j + 1]);
-    const float a0 = fmaf(h0 * rstd, 1.f + sa.lo(), ha.lo());
-    const float a1 = fmaf(h1 * rstd, 1.f + sa.hi(), ha.hi());
-    const float a2 = fmaf(h2 * rstd, 1.f + sb.lo(), hb.lo());
-    const float a3 = fmaf(h3 * rstd, 1.f + sb.hi(), hb.hi());
-    *reinterpret_cast<uint32_t*>(xrow + ca * 2) = live ? pack_bf2(a0, a1) : 0u;
-    *reinterpret_cast<uint32_t*>(xrow + cb * 2) = live ? pack_bf2(a2, a3) : 0u;
-    if (live) {
-      int o = ca - c.c0;
-      if (o >= 0 && o < c.R_h) c.res[n * RESW + o] = h0;
-      if (o + 1 >= 0 && o + 1 < c.R_h) c.res[n * RESW + o + 1] = h1;
-      o = cb - c.c0;
-      if (o >= 0 && o < c.R_h) c.res[n * RESW + o] = h2;
-      if (o + 1 >= 0 && o + 1 < c.R_h) c.res[n * RESW + o + 1] = h3;
-    }
+  float* res = cRes(p, c) + n * RESW;
+#pragma unroll 1
+  for (int j = 0; j < 24; ++j) {  // 24 column pairs: (ca, ca+1) then (ca+8, ca+9) of word pair j / 2
+    const int col = col_a_of(part + 16 * (j >> 1)) + 8 * (j & 1);
+    uint32_t* px = reinterpret_cast<uint32_t*>(xrow + col * 2);
+    const uint32_t u = *px;
+    const float h0 = bf_lo(u), h1 = bf_hi(u);
+    const float2 sc = mod2<ModT>(msc, col), sh = mod2<ModT>(msh, col);
+    const float a0 = fmaf(h0 * rstd, 1.f + sc.x, sh.x);
+    const float a1 = fmaf(h1 * rstd, 1.f + sc.y, sh.y);
+    *px = live ? pack_bf2(a0, a1) : 0u;
+    // c0 and R_h are even: a column pair is entirely inside or outside the residual columns
+    if (live && (unsigned)(col - c.c0) < (unsigned)c.R_h)
+      *reinterpret_cast<float2*>(res + (col - c.c0)) = make_float2(h0, h1);
   }
 }
 
 // ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ void store_partials(const Params& p, const Cta& c, const float (&d0)[4], const float (&d1)[4]) {
+  const int g = c.lane >> 2, cc = c.lane & 3;
+  float* P = cP(p, c) + c.warp * 256;
+  P[g * 16 + 2 * cc] = d0[0];
+  P[g * 16 + 2 * cc + 1] = d0[1];
+  P[(g + 8) * 16 + 2 * cc] = d0[2];
+  P[(g + 8) * 16 + 2 * cc + 1] = d0[3];
+  P[g * 16 + 8 + 2 * cc] = d1[0];
+  P[g * 16 + 8 + 2 * cc + 1] = d1[1];
+  P[(g + 8) * 16 + 8 + 2 * cc] = d1[2];
+  P[(g + 8) * 16 + 8 + 2 * cc + 1] = d1[3];
+}
+
 // GEMM with the B operand (activations) from shared X: `nmat` matrices of R rows each (K = H).
 __device__ void mma_from_x(const Params& p, Cta& c, const char* wslot, int nmat, int R) {
   const int mtpm = (R + 15) >> 4, mt = nmat * mtpm, ks = NW / mt;
@@ -306,8 +376,8 @@ __device__ void mma_from_x(const Params& p, Cta& c, const char* wslot, int nmat,
     const int kb0 = ksl * KB / ks, kb1 = (ksl + 1) * KB / ks;
     const int ra = mm * 16 + g, rb = ra + 8;
     const bool va = ra < R, vb = rb < R;
-    const char* x0 = c.U + (size_t)g * XS * 2 + cc * 4;
-    const char* x1 = c.U + (size_t)(8 + g) * XS * 2 + cc * 4;
+    const char* x0 = cX(p, c) + (size_t)g * XS * 2 + cc * 4;
+    const char* x1 = cX(p, c) + (size_t)(8 + g) * XS * 2 + cc * 4;
 #pragma unroll 4
     for (int kb = kb0; kb < kb1; ++kb) {
       const char* blk = A + (size_t)kb * R * 32;
@@ -321,80 +391,84 @@ __device__ void mma_from_x(const Params& p, Cta& c, const char* wslot, int nmat,
       }
     }
   }
-  float* P = c.P + c.warp * 256;
-  P[g * 16 + 2 * cc] = d0[0];
-  P[g * 16 + 2 * cc + 1] = d0[1];
-  P[(g + 8) * 16 + 2 * cc] = d0[2];
-  P[(g + 8) * 16 + 2 * cc + 1] = d0[3];
-  P[g * 16 + 8 + 2 * cc] = d1[0];
-  P[g * 16 + 8 + 2 * cc + 1] = d1[1];
-  P[(g + 8) * 16 + 8 + 2 * cc] = d1[2];
-  P[(g + 8) * 16 + 8 + 2 * cc + 1] = d1[3];
+  store_partials(p, c, d0, d1);
 }
 
-// GEMM with the B operand polled straight from an exchange buffer (rows of K/2 words); one
-// matrix of R <= 16 rows, K split over the 8 warps. Returns nonzero on a failed wait.
+// GEMM with the B operand polled straight from an exchange buffer (rows of K/2 words); one matrix
+// of R <= 16 rows, K split over the 8 warps, in chunks of CH k-blocks with the next chunk's loads
+// in flight while the current chunk is checked and multiplied. Returns nonzero on a failed wait.
+template <int CH>
+struct WordChunk {
+  u64 w0[2 * CH], w1[2 * CH];
+};
+
 __device__ int mma_from_words(const Params& p, Cta& c, const char* wslot, int R, int K, const u64* rows,
                               uint32_t tag, int stage) {
+  constexpr int CH = 4;
   const int g = c.lane >> 2, cc = c.lane & 3;
   const int RW = K >> 1, KB = K >> 4;
   const int kb0 = c.warp * KB / NW, kb1 = (c.warp + 1) * KB / NW;
   const bool v0 = g < p.T, v1 = (8 + g) < p.T, two = p.T > 8;
   const u64* row0 = rows + (size_t)g * RW + 2 * cc;
-  const u64* row1 = rows + (size_t)(8 + g) * RW + 2 * cc;
+  const size_t d1off = (size_t)8 * RW;  // row 8 + g
   const char* A = wslot + cc * 8;
   const bool va = g < R, vb = g + 8 < R;
   float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
   Waiter wt(p.status, p.timeout_ns);
-  int rc = 0;
-  constexpr int CH = 6;
-  for (int kbc = kb0; kbc < kb1; kbc += CH) {
-    const u64* ptr[2 * CH];
-    u64 w0[2 * CH], w1[2 * CH];
+  const int nch = (kb1 - kb0 + CH - 1) / CH;
+  WordChunk<CH> buf0, buf1;
+  auto issue = [&](WordChunk<CH>& b, int ch) {
+    const int kbase = kb0 + ch * CH;
     uint32_t valid = 0;
 #pragma unroll
-    for (int i = 0; i < CH; ++i) {
-      const int kb = kbc + i;
-      ptr[2 * i] = row0 + kb * 8;
-      ptr[2 * i + 1] = row1 + kb * 8;
-      if (kb < kb1) valid |= ((v0 ? 1u : 0u) | (v1 ? 2u : 0u)) << (2 * i);
-    }
-    rc = poll_pairs<2 * CH>(ptr, w0, w1, valid, tag, wt);
-    if (__any_sync(0xffffffffu, rc != 0)) {  // keep the warp converged for mma.sync
-      if (rc == 0) rc = 2;
-      break;
-    }
+    for (int i = 0; i < CH; ++i)
+      if (kbase + i < kb1) valid |= ((v0 ? 1u : 0u) | (v1 ? 2u : 0u)) << (2 * i);
+    const u64* base = row0 + kbase * 8;
+    issue_pairs<2 * CH>([base, d1off](int i) { return base + (i >> 1) * 8 + ((i & 1) ? d1off : 0); }, b.w0, b.w1,
+                        valid, tag);
+  };
+  auto consume = [&](WordChunk<CH>& b, int ch) -> int {
+    const int kbase = kb0 + ch * CH;
+    const u64* base = row0 + kbase * 8;
+    int rc = complete_pairs<2 * CH>([base, d1off](int i) { return base + (i >> 1) * 8 + ((i & 1) ? d1off : 0); },
+                                    b.w0, b.w1, tag, wt);
+    if (__any_sync(0xffffffffu, rc != 0)) return rc ? rc : 2;  // keep the warp converged for mma.sync
 #pragma unroll
     for (int i = 0; i < CH; ++i) {
-      const int kb = kbc + i;
+      const int kb = kbase + i;
       if (kb < kb1) {
         const char* blk = A + (size_t)kb * R * 32;
         const uint2 a = va ? lds64(blk + g * 32) : make_uint2(0u, 0u);
-        const uint2 b = vb ? lds64(blk + (g + 8) * 32) : make_uint2(0u, 0u);
-        mma_bf16(d0, a.x, b.x, a.y, b.y, payload_of(w0[2 * i]), payload_of(w1[2 * i]));
-        if (two) mma_bf16(d1, a.x, b.x, a.y, b.y, payload_of(w0[2 * i + 1]), payload_of(w1[2 * i + 1]));
+        const uint2 bb = vb ? lds64(blk + (g + 8) * 32) : make_uint2(0u, 0u);
+        mma_bf16(d0, a.x, bb.x, a.y, bb.y, payload_of(b.w0[2 * i]), payload_of(b.w1[2 * i]));
+        if (two) mma_bf16(d1, a.x, bb.x, a.y, bb.y, payload_of(b.w0[2 * i + 1]), payload_of(b.w1[2 * i + 1]));
       }
     }
+    return 0;
+  };
+  int rc = 0;
+  if (nch > 0) issue(buf0, 0);
+  for (int ch = 0; ch < nch; ch += 2) {
+    if (ch + 1 < nch) issue(buf1, ch + 1);
+    rc = consume(buf0, ch);
+    if (rc || ch + 1 >= nch) break;
+    if (ch + 2 < nch) issue(buf0, ch + 2);
+    rc = consume(buf1, ch + 1);
+    if (rc) break;
   }
-  float* P = c.P + c.warp * 256;
-  P[g * 16 + 2 * cc] = d0[0];
-  P[g * 16 + 2 * cc + 1] = d0[1];
-  P[(g + 8) * 16 + 2 * cc] = d0[2];
-  P[(g + 8) * 16 + 2 * cc + 1] = d0[3];
-  P[g * 16 + 8 + 2 * cc] = d1[0];
-  P[g * 16 + 8 + 2 * cc + 1] = d1[1];
-  P[(g + 8) * 16 + 8 + 2 * cc] = d1[2];
-  P[(g + 8) * 16 + 8 + 2 * cc + 1] = d1[3];
+  store_partials(p, c, d0, d1);
   return fail_code(p, c, rc, stage);
 }
 
 // Sum of the K-split partials for output row r (of matrix j), token n.
-__device__ __forceinline__ float part_sum(const Cta& c, int j, int R, int nmat, int r, int n) {
+__device__ __forceinline__ float part_sum(const Params& p, const Cta& c, int j, int R, int nmat, int r, int n) {
   const int mtpm = (R + 15) >> 4, mt = nmat * mtpm, ks = NW / mt;
   const int m = j * mtpm + (r >> 4);
   const int idx = (r & 15) * 16 + n;
+  const float* P = cP(p, c) + m * 256 + idx;
   float s = 0.f;
-  for (int k = 0; k < ks; ++k) s += c.P[(m + mt * k) * 256 + idx];
+#pragma unroll 1
+  for (int k = 0; k < ks; ++k) s += P[mt * k * 256];
   return s;
 }
 
@@ -403,28 +477,28 @@ __device__ __forceinline__ float part_sum(const Cta& c, int j, int R, int nmat, 
 __device__ void epi_plain(const Params& p, const Cta& c, int R, int col0, u64* out_rows, int row_words,
                           uint32_t tag) {
   const int npairs = R >> 1;
-  for (int e = c.tid; e < npairs * p.T; e += NT) {
+  const int e = c.tid;
+  if (e < npairs * p.T) {
     const int pp = e % npairs, n = e / npairs;
-    const float v0 = part_sum(c, 0, R, 1, 2 * pp, n), v1 = part_sum(c, 0, R, 1, 2 * pp + 1, n);
+    const float v0 = part_sum(p, c, 0, R, 1, 2 * pp, n), v1 = part_sum(p, c, 0, R, 1, 2 * pp + 1, n);
     st_volatile(out_rows + (size_t)n * row_words + word_pos((col0 >> 1) + pp), make_word(tag, pack_bf2(v0, v1)));
   }
 }
 
-// Gated residual out = bf16(res + bf16(acc) * gate) (src/mk_expert.py:162-172).
+// Gated residual out = bf16(res + bf16(acc) * gate) (src/mk_expert.py:162-172); gate in shared memory.
 template <typename ModT>
 __device__ void epi_gated(const Params& p, const Cta& c, const ModT* gate, u64* out_rows, uint32_t tag,
                           uint16_t* trace) {
   const int npairs = c.R_h >> 1;
-  for (int e = c.tid; e < npairs * p.T; e += NT) {
+  const int e = c.tid;
+  if (e < npairs * p.T) {
     const int pp = e % npairs, n = e / npairs;
-    float o[2];
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const int r = 2 * pp + k;
-      const float acc = round_bf(part_sum(c, 0, c.R_h, 1, r, n));
-      o[k] = fmaf(acc, mod_at<ModT>(gate, c.c0 + r), c.res[n * RESW + r]);
-    }
-    const uint32_t pl = pack_bf2(o[0], o[1]);
+    const float2 gv = mod2<ModT>(gate, c.c0 + 2 * pp);
+    const float a0 = round_bf(part_sum(p, c, 0, c.R_h, 1, 2 * pp, n));
+    const float a1 = round_bf(part_sum(p, c, 0, c.R_h, 1, 2 * pp + 1, n));
+    const float o0 = fmaf(a0, gv.x, cRes(p, c)[n * RESW + 2 * pp]);
+    const float o1 = fmaf(a1, gv.y, cRes(p, c)[n * RESW + 2 * pp + 1]);
+    const uint32_t pl = pack_bf2(o0, o1);
     st_volatile(out_rows + (size_t)n * HWORDS + word_pos((c.c0 >> 1) + pp), make_word(tag, pl));
     if (trace) *reinterpret_cast<uint32_t*>(trace + (size_t)n * H + c.c0 + 2 * pp) = pl;
   }
@@ -433,15 +507,16 @@ __device__ void epi_gated(const Params& p, const Cta& c, const ModT* gate, u64* 
 // g = bf16(silu(bf16(gate)) * bf16(up)) (src/mk_expert.py:403-413).
 __device__ void epi_gu(const Params& p, const Cta& c, u64* out_rows, uint32_t tag) {
   const int R = c.R_gu, npairs = R >> 1, row_words = p.I >> 1;
-  for (int e = c.tid; e < npairs * p.T; e += NT) {
+  const int e = c.tid;
+  if (e < npairs * p.T) {
     const int pp = e % npairs, n = e / npairs;
     float o[2];
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
       const int r = 2 * pp + k;
-      const float gf = round_bf(part_sum(c, 0, R, 2, r, n));
-      const float uf = round_bf(part_sum(c, 1, R, 2, r, n));
-      o[k] = gf / (1.f + __expf(-gf)) * uf;
+      const float gf = round_bf(part_sum(p, c, 0, R, 2, r, n));
+      const float uf = round_bf(part_sum(p, c, 1, R, 2, r, n));
+      o[k] = __fdividef(gf, 1.f + __expf(-gf)) * uf;
     }
     st_volatile(out_rows + (size_t)n * row_words + word_pos((c.u0 >> 1) + pp), make_word(tag, pack_bf2(o[0], o[1])));
   }
@@ -463,11 +538,12 @@ __device__ __forceinline__ void bf_words_to_lane(Lane8& x, uint32_t w0, uint32_t
 }
 // Natural-order bf16 row chunk (dims d0..d0+3 in A, d0+8..d0+11 in B) to lane order.
 __device__ __forceinline__ void bf_nat_to_lane(Lane8& x, uint2 A, uint2 B) { bf_words_to_lane(x, A.x, B.x, A.y, B.y); }
-__device__ __forceinline__ void f32_nat_to_lane(Lane8& x, const float* row, int d0) {
-  const float4 A = __ldg(reinterpret_cast<const float4*>(row + d0));
-  const float4 B = __ldg(reinterpret_cast<const float4*>(row + d0 + 8));
+__device__ __forceinline__ void f32_nat_to_lane(Lane8& x, float4 A, float4 B) {
   x.v[0] = A.x; x.v[1] = A.y; x.v[2] = B.x; x.v[3] = B.y;
   x.v[4] = A.z; x.v[5] = A.w; x.v[6] = B.z; x.v[7] = B.w;
+}
+__device__ __forceinline__ void f32_lane_pin(Lane8& x, const float* row, int d0) {
+  f32_nat_to_lane(x, ldg_f4_pin(row + d0), ldg_f4_pin(row + d0 + 8));
 }
 __device__ __forceinline__ float group8_sum(float s) {
   s += __shfl_xor_sync(0xffffffffu, s, 1);
@@ -499,24 +575,23 @@ __device__ __forceinline__ float dot8(const Lane8& a, const Lane8& b) {
   return group8_sum(s);
 }
 // Block-wide max of a value that is uniform within each 8-lane group.
-__device__ __forceinline__ float block_max(const Cta& c, float v) {
+__device__ __forceinline__ float block_max(const Params& p, const Cta& c, float v) {
   v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 8));
   v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 16));
   __syncthreads();
-  if (c.lane == 0) c.red[c.warp] = v;
+  if (c.lane == 0) cRed(p, c)[c.warp] = v;
   __syncthreads();
-  float m = c.red[0];
+  float m = cRed(p, c)[0];
 #pragma unroll
-  for (int w = 1; w < NW; ++w) m = fmaxf(m, c.red[w]);
+  for (int w = 1; w < NW; ++w) m = fmaxf(m, cRed(p, c)[w]);
   return m;
 }
 
 // SA = true: self-attention (queries of row t over memory rows [cu_kv[0], PM) and the T action
 // rows, src/mk_expert.py:196-222). SA = false: cross-attention over the S valid source rows
 // (src/mk_expert.py:225-251). Returns nonzero on a failed wait.
-template <bool SA>
-__device__ int attention_unit(const Params& p, Cta& c, int l, int h, int t, const u64* src_rows, u64* y_rows,
-                              uint32_t tag) {
+__device__ __forceinline__ int attention_unit(const Params& p, Cta& c, const bool SA, int l, int h, int t,
+                                              const u64* src_rows, u64* y_rows, uint32_t tag) {
   const int kg = c.tid >> 3, l8 = c.tid & 7;
   const int d0 = 16 * (l8 >> 1) + 4 * (l8 & 1);
   const int nkeys = SA ? p.mem_rows : min(__ldg(p.cu_src + 1), p.ca_rows);
@@ -528,7 +603,8 @@ __device__ int attention_unit(const Params& p, Cta& c, int l, int h, int t, cons
   const float* cosr = (SA ? p.sa_cos : p.ca_cos);
   const float* sinr = (SA ? p.sa_sin : p.ca_sin);
 
-  // Prefetch chunk 0 of K/V and the per-row tables; none of it depends on the exchange.
+  // Load chunk 0 of K/V and the per-row tables; none of it depends on the exchange, and the pinned
+  // loads are in flight while the query is polled.
   uint2 kA[MAXK], kB[MAXK], vA[MAXK], vB[MAXK];
   auto load_chunk = [&](int base) {
 #pragma unroll
@@ -538,40 +614,37 @@ __device__ int attention_unit(const Params& p, Cta& c, int l, int h, int t, cons
       if (j < nkeys) {
         const uint16_t* kr = Kb + (size_t)j * stride + h * HD + d0;
         const uint16_t* vr = Vb + (size_t)j * stride + h * HD + d0;
-        kA[i] = __ldg(reinterpret_cast<const uint2*>(kr));
-        kB[i] = __ldg(reinterpret_cast<const uint2*>(kr + 8));
-        vA[i] = __ldg(reinterpret_cast<const uint2*>(vr));
-        vB[i] = __ldg(reinterpret_cast<const uint2*>(vr + 8));
+        kA[i] = ldg_u2_pin(kr);
+        kB[i] = ldg_u2_pin(kr + 8);
+        vA[i] = ldg_u2_pin(vr);
+        vB[i] = ldg_u2_pin(vr + 8);
       }
     }
   };
   load_chunk(kbeg);
   Lane8 wq, cq, sq;
-  f32_nat_to_lane(wq, nrm, d0);
-  f32_nat_to_lane(cq, cosr + (size_t)t * HD, d0);
-  f32_nat_to_lane(sq, sinr + (size_t)t * HD, d0);
+  f32_lane_pin(wq, nrm, d0);
+  f32_lane_pin(cq, cosr + (size_t)t * HD, d0);
+  f32_lane_pin(sq, sinr + (size_t)t * HD, d0);
   const bool own = SA && kg < p.T;
   Lane8 wk, ck, sk;
   if (SA) {
-    f32_nat_to_lane(wk, nrm + (size_t)p.L * HD, d0);
     const int krow = kg < p.T ? kg : p.T - 1;  // groups without an own row compute a discarded key
-    f32_nat_to_lane(ck, cosr + (size_t)krow * HD, d0);
-    f32_nat_to_lane(sk, sinr + (size_t)krow * HD, d0);
+    f32_lane_pin(wk, nrm + (size_t)p.L * HD, d0);
+    f32_lane_pin(ck, cosr + (size_t)krow * HD, d0);
+    f32_lane_pin(sk, sinr + (size_t)krow * HD, d0);
   }
 
   // Poll the query (and, for SA, this group's own action row's k and v).
   const int qoff = h * 32 + 4 * l8;
   const int row_words = SA ? QKVWORDS : HWORDS;
-  const u64* ptr[6];
   u64 w0[6], w1[6];
-  ptr[0] = src_rows + (size_t)t * row_words + qoff;
-  ptr[1] = ptr[0] + 2;
-  ptr[2] = src_rows + (size_t)kg * row_words + HWORDS + qoff;
-  ptr[3] = ptr[2] + 2;
-  ptr[4] = src_rows + (size_t)kg * row_words + 2 * HWORDS + qoff;
-  ptr[5] = ptr[4] + 2;
+  const u64* qrow = src_rows + (size_t)t * row_words + qoff;
+  const u64* krow = src_rows + (size_t)kg * row_words + HWORDS + qoff;  // k at +HWORDS, v at +2 HWORDS
+  auto addr = [qrow, krow](int i) { return (i < 2 ? qrow : krow + (i >> 2) * HWORDS) + 2 * (i & 1); };
   Waiter wt(p.status, p.timeout_ns);
-  const int rc = poll_pairs<6>(ptr, w0, w1, own ? 0x3fu : 0x3u, tag, wt);
+  issue_pairs<6>(addr, w0, w1, own ? 0x3fu : 0x3u, tag);
+  const int rc = complete_pairs<6>(addr, w0, w1, tag, wt);
   fail_code(p, c, rc, SA ? ST_SA : ST_CA);
   if (__syncthreads_or(rc != 0)) return 1;
 
@@ -609,7 +682,7 @@ __device__ int attention_unit(const Params& p, Cta& c, int l, int h, int t, cons
       s[i] = j < nkeys ? dv : -INFINITY;
       mloc = fmaxf(mloc, s[i]);
     }
-    const float m_new = fmaxf(m_run, block_max(c, mloc));
+    const float m_new = fmaxf(m_run, block_max(p, c, mloc));
     const float alpha = __expf(m_run - m_new);  // 0 on the first chunk
     den *= alpha;
 #pragma unroll
@@ -639,8 +712,8 @@ __device__ int attention_unit(const Params& p, Cta& c, int l, int h, int t, cons
   }
   // Reduce the 32 groups: o in lane order per lane, den per group.
   __syncthreads();
-  float* ro = c.P;            // [32][64]
-  float* rd = c.P + 32 * 64;  // [32]
+  float* ro = cP(p, c);            // [32][64]
+  float* rd = cP(p, c) + 32 * 64;  // [32]
 #pragma unroll
   for (int e = 0; e < 8; ++e) ro[kg * 64 + l8 * 8 + e] = o[e];
   if (l8 == 0) rd[kg] = den;
@@ -660,133 +733,258 @@ __device__ int attention_unit(const Params& p, Cta& c, int l, int h, int t, cons
 }
 
 // ---------------------------------------------------------------------------------------------
-// Step tail (src/mk_expert.py:254-299). Thread (n, part) owns the 48 columns of its word pairs.
-// mode 0: FIRST (h0 from x_in), 1: intermediate step (velocity, Euler update, h0), 2: last step
-// (CTA a < A writes output dim a). Produces hv (h0 payloads) for modes 0 and 1.
+// Step tail (src/mk_expert.py:254-299), split in two:
+//
+// velocity_row: CTA n < T, action row n. o = bf16(AdaRMS_final(h[n])) (final-norm scale/shift from
+// the modulation ring), v_a = o . Wout[a] + bout[a] in fp32, x_a <- xpad_a + dt v_a. Thread t < 192
+// owns the 4 columns of word pair t of row n. Intermediate steps publish x_a (a < action_dim) as
+// tagged fp32 words; the last step writes x_out[n][0..A) (dims >= action_dim: 0 + dt v_a).
 template <typename ModT>
-__device__ int step_tail(const Params& p, Cta& c, int mode, const ModT* modf, const u64* hrows, uint32_t htag,
-                         uint32_t (&hv)[24]) {
-  const int n = c.tid >> 4, part = c.tid & 15;
-  const float* tw = reinterpret_cast<const float*>(c.U);
-  const float* s_wout = tw;
-  const float* s_win = tw + AO * H;
-  const float* s_bin = tw + 2 * AO * H;
-  const float* s_bout = s_bin + H;
+__device__ int velocity_row(const Params& p, Cta& c, int n, bool last, const ModT* mfin, const u64* hrows,
+                            uint32_t htag, u64* xrows, uint32_t xtag) {
+  const int t = c.tid;
+  const bool act = t < HWORDS / 2;
+  const int ca = col_a_of(act ? t : 0);
   const float dt = __ldg(p.dt);
-  const int adim = p.adim;
-  const int a_out = c.cta;  // output dim of this CTA in mode 2
-  if (mode == 2 && a_out >= p.A) return 0;  // uniform per CTA: only CTAs 0..A-1 write the output
-  float wrow[48];
-  if (mode == 2) {
+  float2 wa[AO], wb[AO];
+  const int ndim = last ? p.A : p.adim;
+  if (!last) {
 #pragma unroll
-    for (int j = 0; j < 12; ++j) {
-      const int ca = col_a_of(part + 16 * j);
-      const float2 A = __ldg(reinterpret_cast<const float2*>(p.wout + (size_t)a_out * H + ca));
-      const float2 B = __ldg(reinterpret_cast<const float2*>(p.wout + (size_t)a_out * H + ca + 8));
-      wrow[4 * j] = A.x; wrow[4 * j + 1] = A.y; wrow[4 * j + 2] = B.x; wrow[4 * j + 3] = B.y;
+    for (int a = 0; a < AO; ++a) {
+      const bool ok = act && a < ndim;
+      wa[a] = ok ? ldg_f2_pin(p.wout + (size_t)a * H + ca) : make_float2(0.f, 0.f);
+      wb[a] = ok ? ldg_f2_pin(p.wout + (size_t)a * H + ca + 8) : make_float2(0.f, 0.f);
     }
   }
-  float xo[AO];
-  if (mode != 0) {
-    // o = bf16(AdaRMS_final(h)), v_a = o . Wout[a] + bout[a]
-    ModPair<ModT> sa[12], sb[12], ha[12], hb[12];
-#pragma unroll
-    for (int j = 0; j < 12; ++j) {
-      const int ca = col_a_of(part + 16 * j);
-      sa[j].load(modf, ca); sb[j].load(modf, ca + 8);
-      ha[j].load(modf + H, ca); hb[j].load(modf + H, ca + 8);
+  u64 w0 = make_word(htag, 0u), w1 = w0;
+  Waiter wt(p.status, p.timeout_ns);
+  int rc = 0;
+  if (act) {
+    const u64* ptr = hrows + (size_t)n * HWORDS + 2 * t;
+    ld_volatile_v2(ptr, w0, w1);
+    while (rc == 0 && (tag_of(w0) != htag || tag_of(w1) != htag)) {
+      rc = wt.tick();
+      ld_volatile_v2(ptr, w0, w1);
     }
-    const int rc = load_rows_poll<ModT>(p, c, hrows, htag, hv, ST_TAIL);
-    if (__syncthreads_or(rc)) return 1;
-    float ss = 0.f;
+  }
+  fail_code(p, c, rc, ST_TAIL);
+  if (__syncthreads_or(rc != 0)) return 1;
+  const float h0 = bf_lo(payload_of(w0)), h1 = bf_hi(payload_of(w0));
+  const float h2 = bf_lo(payload_of(w1)), h3 = bf_hi(payload_of(w1));
+  float ss = h0 * h0 + h1 * h1 + h2 * h2 + h3 * h3;
 #pragma unroll
-    for (int j = 0; j < 24; ++j) {
-      const float a = bf_lo(hv[j]), b = bf_hi(hv[j]);
-      ss = fmaf(a, a, ss);
-      ss = fmaf(b, b, ss);
-    }
-    ss += __shfl_xor_sync(0xffffffffu, ss, 8);
-    ss += __shfl_xor_sync(0xffffffffu, ss, 4);
-    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-    const float rstd = rsqrtf(ss / (float)H + p.eps);
-    float ov[48];
+  for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (c.lane == 0) cRed(p, c)[c.warp] = ss;
+  __syncthreads();
+  ss = 0.f;
 #pragma unroll
-    for (int j = 0; j < 12; ++j) {
-      ov[4 * j] = round_bf(fmaf(bf_lo(hv[2 * j]) * rstd, 1.f + sa[j].lo(), ha[j].lo()));
-      ov[4 * j + 1] = round_bf(fmaf(bf_hi(hv[2 * j]) * rstd, 1.f + sa[j].hi(), ha[j].hi()));
-      ov[4 * j + 2] = round_bf(fmaf(bf_lo(hv[2 * j + 1]) * rstd, 1.f + sb[j].lo(), hb[j].lo()));
-      ov[4 * j + 3] = round_bf(fmaf(bf_hi(hv[2 * j + 1]) * rstd, 1.f + sb[j].hi(), hb[j].hi()));
-    }
-    if (mode == 2) {
-      float acc = 0.f;
+  for (int w = 0; w < NW; ++w) ss += cRed(p, c)[w];
+  const float rstd = rsqrtf(ss / (float)H + p.eps);
+  const float2 sa = mod2<ModT>(mfin, ca), sb = mod2<ModT>(mfin, ca + 8);
+  const float2 ha = mod2<ModT>(mfin + H, ca), hb = mod2<ModT>(mfin + H, ca + 8);
+  const float o0 = act ? round_bf(fmaf(h0 * rstd, 1.f + sa.x, ha.x)) : 0.f;
+  const float o1 = act ? round_bf(fmaf(h1 * rstd, 1.f + sa.y, ha.y)) : 0.f;
+  const float o2 = act ? round_bf(fmaf(h2 * rstd, 1.f + sb.x, hb.x)) : 0.f;
+  const float o3 = act ? round_bf(fmaf(h3 * rstd, 1.f + sb.y, hb.y)) : 0.f;
+  float* vred = cRed(p, c) + 16;  // [NW][AO]
+  for (int a0 = 0; a0 < ndim; a0 += AO) {
+    if (last) {
 #pragma unroll
-      for (int e = 0; e < 48; ++e) acc = fmaf(ov[e], wrow[e], acc);
-      acc += __shfl_xor_sync(0xffffffffu, acc, 8);
-      acc += __shfl_xor_sync(0xffffffffu, acc, 4);
-      acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-      const float v = acc + __ldg(p.tailw + 2 * AO * H + H + a_out);
-      if (part == 0 && n < p.T) {
-        const float xp = a_out < adim ? c.xs[n * 32 + a_out] : 0.f;
-        p.x_out[(size_t)n * p.A + a_out] = fmaf(dt, v, xp);
+      for (int a = 0; a < AO; ++a) {
+        const bool ok = act && a0 + a < ndim;
+        wa[a] = ok ? ldg_f2_pin(p.wout + (size_t)(a0 + a) * H + ca) : make_float2(0.f, 0.f);
+        wb[a] = ok ? ldg_f2_pin(p.wout + (size_t)(a0 + a) * H + ca + 8) : make_float2(0.f, 0.f);
       }
-      return 0;
     }
 #pragma unroll
     for (int a = 0; a < AO; ++a) {
-      float acc = 0.f;
-      if (a < adim) {
-        const float* wr = s_wout + a * H;
+      float acc = o0 * wa[a].x;
+      acc = fmaf(o1, wa[a].y, acc);
+      acc = fmaf(o2, wb[a].x, acc);
+      acc = fmaf(o3, wb[a].y, acc);
 #pragma unroll
-        for (int j = 0; j < 12; ++j) {
-          const int ca = col_a_of(part + 16 * j);
-          acc = fmaf(ov[4 * j], wr[ca], acc);
-          acc = fmaf(ov[4 * j + 1], wr[ca + 1], acc);
-          acc = fmaf(ov[4 * j + 2], wr[ca + 8], acc);
-          acc = fmaf(ov[4 * j + 3], wr[ca + 9], acc);
-        }
-      }
-      acc += __shfl_xor_sync(0xffffffffu, acc, 8);
-      acc += __shfl_xor_sync(0xffffffffu, acc, 4);
-      acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-      const float v = acc + s_bout[a];
-      xo[a] = a < adim ? fmaf(dt, v, c.xs[n * 32 + a]) : 0.f;
+      for (int o = 16; o >= 1; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (c.lane == 0) vred[c.warp * AO + a] = acc;
     }
-    __syncwarp();
-    if (part == 0 && n < p.T) {
+    __syncthreads();
+    if (t < AO && a0 + t < ndim) {
+      const int a = a0 + t;
+      float v = 0.f;
 #pragma unroll
-      for (int a = 0; a < AO; ++a)
-        if (a < adim) c.xs[n * 32 + a] = xo[a];
+      for (int w = 0; w < NW; ++w) v += vred[w * AO + t];
+      v += __ldg(p.tailw + AO * H + H + a);
+      const float xp = a < p.adim ? cXs(p, c)[n * 32 + a] : 0.f;
+      const float xn = fmaf(dt, v, xp);
+      if (last)
+        p.x_out[(size_t)n * p.A + a] = xn;
+      else
+        st_volatile(xrows + (size_t)n * XWORDS + a, make_word(xtag, __float_as_uint(xn)));
     }
-  } else {
-#pragma unroll
-    for (int a = 0; a < AO; ++a) xo[a] = (a < adim && n < p.T) ? c.xs[n * 32 + a] : 0.f;
-  }
-  // h0 = bf16(xpad[:AO] @ Win[:AO] + bin) in fp32.
-#pragma unroll
-  for (int j = 0; j < 12; ++j) {
-    const int ca = col_a_of(part + 16 * j);
-    float hq[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int col = ca + (e & 1) + (e >> 1) * 8;
-      float acc = s_bin[col];
-#pragma unroll
-      for (int a = 0; a < AO; ++a) acc = fmaf(xo[a], s_win[a * H + col], acc);
-      hq[e] = acc;
-    }
-    hv[2 * j] = n < p.T ? pack_bf2(hq[0], hq[1]) : 0u;
-    hv[2 * j + 1] = n < p.T ? pack_bf2(hq[2], hq[3]) : 0u;
+    __syncthreads();
   }
   return 0;
 }
 
+// Every CTA: the new action state from the exchange (intermediate steps). Returns nonzero (CTA-
+// uniform) on a failed wait.
+__device__ int take_new_x(const Params& p, Cta& c, const u64* xrows, uint32_t xtag) {
+  const int t = c.tid;
+  const int n = t >> 3, a = t & 7;
+  int rc = 0;
+  if (n < p.T && a < p.adim) {
+    Waiter wt(p.status, p.timeout_ns);
+    u64 w;
+    rc = poll_word(xrows + (size_t)n * XWORDS + a, w, xtag, wt);
+    if (rc == 0) cXs(p, c)[n * 32 + a] = __uint_as_float(payload_of(w));
+  }
+  fail_code(p, c, rc, ST_TAIL);
+  return __syncthreads_or(rc != 0);
+}
+
+// In-projection h0 = bf16(xpad[:AO] @ Win[:AO] + bin) in fp32 (src/mk_expert.py:280-293) into X
+// (natural layout); thread t owns columns t, t + 256, t + 512, whose Win / bin values it loads
+// up front.
+__device__ __forceinline__ void load_inproj(const Params& p, const Cta& c, float (&win)[3][AO], float (&bin)[3]) {
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    const int col = c.tid + NT * k;
+#pragma unroll
+    for (int a = 0; a < AO; ++a) win[k][a] = ldg_f1_pin(p.tailw + (size_t)a * H + col);
+    bin[k] = ldg_f1_pin(p.tailw + AO * H + col);
+  }
+}
+
+__device__ void in_proj_to_x(const Params& p, Cta& c, const float (&win)[3][AO], const float (&bin)[3]) {
+#pragma unroll 1
+  for (int n = 0; n < TP; ++n) {
+    float xp[AO];
+#pragma unroll
+    for (int a = 0; a < AO; ++a) xp[a] = (a < p.adim && n < p.T) ? cXs(p, c)[n * 32 + a] : 0.f;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      float acc = bin[k];
+#pragma unroll
+      for (int a = 0; a < AO; ++a) acc = fmaf(xp[a], win[k][a], acc);
+      reinterpret_cast<__nv_bfloat16*>(cX(p, c))[(size_t)n * XS + c.tid + NT * k] =
+          __float2bfloat16_rn(n < p.T ? acc : 0.f);
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------------------------
+// Stage routines. The per-layer loop below calls each routine from exactly one place, so each
+// distinct stage exists once in the binary: the loop's code stays resident in the SM instruction
+// cache instead of being re-fetched from L2 every layer. Each returns nonzero (CTA-uniform) after a
+// failed wait.
+
+// AdaRMS + GEMM stages. which = 0: QKV of AdaRMS(h; sa) (h from the previous layer, or from X for
+// layer 0, where the step tail left h0); 1: CA query of AdaRMS(h2; ca); 2: gate/up of
+// AdaRMS(h3; mlp) with g = bf16(silu(bf16(gate)) * bf16(up)).
+template <typename ModT>
+__device__ __forceinline__ int stage_norm_gemm(const Params& p, Cta& c, int which, int gi, int l, int q) {
+  const int par = gi & 1;
+  const uint32_t tag = c.tag0 + (uint32_t)gi;
+  u64* const* xb = p.xb;
+  if (!(which == 0 && l == 0)) {  // layer 0's h0 is already in X (step tail)
+    const u64* rows = which == 0 ? xb[B_HOUT] + (size_t)((gi - 1) & 1) * TP * HWORDS
+                                 : xb[which == 1 ? B_H2 : B_H3] + (size_t)par * TP * HWORDS;
+    const int fail = poll_rows_to_x(p, c, rows, which == 0 ? tag - 1u : tag, ST_QKV + 3 * which);
+    if (__syncthreads_or(fail)) return 1;
+  }
+  int fail = !wait_bar(p, c, BAR_MODS + (q & 1));
+  if (__syncthreads_or(fail)) return 1;
+  consumed(p, c, BAR_MODS + (q & 1));
+  stage_adarms<ModT>(p, c, mods_slot<ModT>(p, c, q));
+  const int slot = which == 0 ? S_QKV : (which == 1 ? S_QCA : S_GU);
+  fail = !wait_bar(p, c, slot);
+  if (__syncthreads_or(fail)) return 1;
+  consumed(p, c, slot);
+  const int R = which == 0 ? c.R_qkv : (which == 1 ? c.R_h : c.R_gu);
+  mma_from_x(p, c, cSlot(p, c, slot), which == 2 ? 2 : 1, R);
+  __syncthreads();
+  if (c.tid == ISSUER && gi + 1 < p.n_steps * p.L) issue_slot(p, c, slot, (gi + 1) % p.L);
+  if (which == 2) {
+    epi_gu(p, c, xb[B_G] + (size_t)par * TP * (p.I >> 1), tag);
+  } else if (which == 1) {
+    epi_plain(p, c, c.R_h, c.c0, xb[B_QCA] + (size_t)par * TP * HWORDS, HWORDS, tag);
+  } else if (!(p.drop_stage == ST_QKV && c.cta == 0 && gi == 0)) {
+    epi_plain(p, c, c.R_qkv, c.r0_qkv, xb[B_QKV] + (size_t)par * TP * QKVWORDS, QKVWORDS, tag);
+  }
+  return 0;
+}
+
+// GEMM stages fed straight from an exchange buffer, with a gated-residual epilogue.
+// which = 0: h2 = bf16(h + bf16(y @ Wo^T) * gate_sa); 1: h3 = bf16(h2 + bf16(y_ca @ Woca^T) * gate_ca);
+// 2: h = bf16(h3 + bf16(g @ Wd^T) * gate_mlp). q: the modulation block holding the gate.
+template <typename ModT>
+__device__ __forceinline__ int stage_words_gemm(const Params& p, Cta& c, int which, int gi, int q) {
+  const int par = gi & 1;
+  const uint32_t tag = c.tag0 + (uint32_t)gi;
+  u64* const* xb = p.xb;
+  const int slot = which == 0 ? S_O : (which == 1 ? S_OCA : S_D);
+  const int K = which == 2 ? p.I : H;
+  const u64* rows = which == 2 ? xb[B_G] + (size_t)par * TP * (p.I >> 1)
+                               : xb[which == 0 ? B_Y : B_YCA] + (size_t)par * TP * HWORDS;
+  __syncthreads();
+  int fail = !wait_bar(p, c, slot);
+  if (__syncthreads_or(fail)) return 1;
+  consumed(p, c, slot);
+  fail = mma_from_words(p, c, cSlot(p, c, slot), c.R_h, K, rows, tag, ST_O + 3 * which);
+  if (__syncthreads_or(fail)) return 1;
+  if (c.tid == ISSUER && gi + 1 < p.n_steps * p.L) issue_slot(p, c, slot, (gi + 1) % p.L);
+  u64* out = xb[which == 0 ? B_H2 : (which == 1 ? B_H3 : B_HOUT)] + (size_t)par * TP * HWORDS;
+  epi_gated<ModT>(p, c, mods_slot<ModT>(p, c, q) + 2 * H, out, tag,
+                  (which == 2 && p.trace_h) ? p.trace_h + (size_t)gi * p.T * H : nullptr);
+  __syncthreads();
+  if (c.tid == ISSUER) issue_mods<ModT>(p, c, q + 2);  // this block's last use
+  return 0;
+}
+
+// Self-attention (sa) or cross-attention, one (head, row) unit per CTA; one routine for both.
+__device__ __forceinline__ int stage_attention(const Params& p, Cta& c, const bool sa, int gi, int l) {
+  const int par = gi & 1;
+  const uint32_t tag = c.tag0 + (uint32_t)gi;
+  const u64* src = sa ? p.xb[B_QKV] + (size_t)par * TP * QKVWORDS : p.xb[B_QCA] + (size_t)par * TP * HWORDS;
+  u64* y = p.xb[sa ? B_Y : B_YCA] + (size_t)par * TP * HWORDS;
+  for (int u = c.cta; u < NH * p.T; u += c.G) {
+    const int fail = attention_unit(p, c, sa, l, u % NH, u / NH, src, y, tag);
+    if (__syncthreads_or(fail)) return 1;
+  }
+  return 0;
+}
+
+// Euler step tail of step s: velocity rows (CTAs n < T), action-state exchange, and every CTA's
+// in-projection of the next step's h0 into X.
+template <typename ModT>
+__device__ __forceinline__ int stage_tail(const Params& p, Cta& c, int s) {
+  const int L = p.L;
+  const int gl = s * L + L - 1;
+  const int q_fin = s * (3 * L + 1) + 3 * L;
+  const bool last = s + 1 == p.n_steps;
+  const uint32_t tl = c.tag0 + (uint32_t)gl;
+  u64* xrows = p.xb[B_X] + (size_t)(gl & 1) * TP * XWORDS;
+  int fail = !wait_bar(p, c, BAR_MODS + (q_fin & 1));
+  if (__syncthreads_or(fail)) return 1;
+  consumed(p, c, BAR_MODS + (q_fin & 1));
+  if (c.cta < p.T) {
+    fail = velocity_row<ModT>(p, c, c.cta, last, mods_slot<ModT>(p, c, q_fin),
+                              p.xb[B_HOUT] + (size_t)(gl & 1) * TP * HWORDS, tl, xrows, tl) != 0;
+    if (__syncthreads_or(fail)) return 1;
+  }
+  __syncthreads();
+  if (c.tid == ISSUER) issue_mods<ModT>(p, c, q_fin + 2);
+  if (!last) {
+    float win[3][AO], bin[3];
+    load_inproj(p, c, win, bin);  // in flight while the new action state is polled
+    if (take_new_x(p, c, xrows, tl)) return 1;
+    in_proj_to_x(p, c, win, bin);
+    __syncthreads();
+  }
+  return 0;
+}
+
 template <typename ModT>
 __global__ void __launch_bounds__(NT, 1) expert_kernel(const __grid_constant__ Params p) {
-  extern __shared__ __align__(1024) char smem[];
   Cta c;
   c.tid = threadIdx.x;
   c.warp = c.tid >> 5;
@@ -794,15 +992,6 @@ __global__ void __launch_bounds__(NT, 1) expert_kernel(const __grid_constant__ P
   c.cta = blockIdx.x;
   c.G = gridDim.x;
   c.stages = 0;
-#pragma unroll
-  for (int s = 0; s < NSLOT; ++s) c.slot[s] = smem + p.s_slot[s];
-  c.U = smem + p.s_u;
-  c.P = reinterpret_cast<float*>(smem + p.s_p);
-  c.xs = reinterpret_cast<float*>(smem + p.s_x);
-  c.res = reinterpret_cast<float*>(smem + p.s_res);
-  c.red = reinterpret_cast<float*>(smem + p.s_red);
-  c.bar = reinterpret_cast<uint64_t*>(smem + p.s_bar);
-  c.cnt = reinterpret_cast<int*>(smem + p.s_cnt);
   {
     const int G = c.G, i = c.cta;
     int lo = part_lo(i, 3 * H / 2, G), hi = part_lo(i + 1, 3 * H / 2, G);
@@ -811,184 +1000,78 @@ __global__ void __launch_bounds__(NT, 1) expert_kernel(const __grid_constant__ P
     c.c0 = 2 * lo; c.R_h = 2 * (hi - lo);
     lo = part_lo(i, p.I / 2, G); hi = part_lo(i + 1, p.I / 2, G);
     c.u0 = 2 * lo; c.R_gu = 2 * (hi - lo);
-    c.slot_bytes[S_QKV] = (uint32_t)c.R_qkv * H * 2;
-    c.slot_bytes[S_O] = c.slot_bytes[S_QCA] = c.slot_bytes[S_OCA] = (uint32_t)c.R_h * H * 2;
-    c.slot_bytes[S_GU] = (uint32_t)c.R_gu * H * 4;
-    c.slot_bytes[S_D] = (uint32_t)c.R_h * p.I * 2;
   }
+  if (p.prof != nullptr && c.tid == 0) p.prof[(size_t)c.cta * (2 + p.n_steps * (8 * p.L + 1))] = globaltimer();
   const uint32_t seq = (uint32_t)ld_volatile_i32(p.status + 1);
   c.tag0 = seq * (uint32_t)MAX_STEP_TAGS + 1u;
   const int L = p.L;
-  const int total = p.n_steps * L;
-  const size_t MODW = (size_t)9 * L * H + 2 * H;
-  const ModT* mods = reinterpret_cast<const ModT*>(p.mods);
-  bool fail = false;
+  const int per = 3 * L + 1;  // modulation blocks per Euler step
 
   if (c.tid == 0) {
-    for (int b = 0; b < NSLOT + 1; ++b) {
-      mbar_init(&c.bar[b], 1);
-      c.cnt[b] = 0;
-      c.cnt[NSLOT + 1 + b] = 0;
+    for (int b = 0; b < NBAR; ++b) {
+      mbar_init(&cBar(p, c)[b], 1);
+      cCnt(p, c)[b] = 0;
+      cCnt(p, c)[NBAR + b] = 0;
     }
     fence_mbar_init();
   }
-  if (c.tid < TP * 32) c.xs[c.tid] = 0.f;
+  if (c.tid < TP * 32) cXs(p, c)[c.tid] = 0.f;
   __syncthreads();
-  if (c.tid == 0) {
-    issue_tail(p, c);
+  if (c.tid == ISSUER) {
     for (int s = 0; s < NSLOT; ++s) issue_slot(p, c, s, 0);
+    issue_mods<ModT>(p, c, 0);
+    issue_mods<ModT>(p, c, 1);
   }
-  for (int e = c.tid; e < p.T * p.A; e += NT) c.xs[(e / p.A) * 32 + (e % p.A)] = __ldg(p.x_in + e);
-  __syncthreads();
+  {
+    // FIRST tail: h0 from the action state after step 1, into X.
+    float win[3][AO], bin[3];
+    load_inproj(p, c, win, bin);
+    for (int e = c.tid; e < p.T * p.A; e += NT) cXs(p, c)[(e / p.A) * 32 + (e % p.A)] = __ldg(p.x_in + e);
+    __syncthreads();
+    in_proj_to_x(p, c, win, bin);
+    __syncthreads();
+  }
+  stage_done(p, c);
 
-  uint32_t hv[24];
-  // FIRST tail: h0 from x after step 1.
-  fail = !wait_bar(p, c, NSLOT);
-  if (__syncthreads_or(fail)) goto drain;
-  consumed(c, NSLOT);
-  step_tail<ModT>(p, c, 0, nullptr, nullptr, 0u, hv);
-  c.stages++;
-  __syncthreads();  // the tail weights in U are dead from here; X takes U over
-
+  // Stage sequence of one layer (src/mk_expert.py:342-421): 0 QKV, 1 SA, 2 SA out, 3 CA query,
+  // 4 CA, 5 CA out, 6 gate/up, 7 down; then, after the last layer, the step tail (8).
   for (int s = 0; s < p.n_steps; ++s) {
-    const ModT* mrow = mods + (size_t)(1 + s) * MODW;
     for (int l = 0; l < L; ++l) {
       const int gi = s * L + l;
-      const int par = gi & 1;
-      const uint32_t tag = c.tag0 + (uint32_t)gi;
-      const ModT* m_sa = mrow + (size_t)9 * l * H;
-      const ModT* m_ca = m_sa + 3 * H;
-      const ModT* m_mlp = m_ca + 3 * H;
-      u64* const* xb = p.xb;
-
-      // 1. QKV = bf16(AdaRMS(h; sa) @ Wqkv^T)
-      if (l > 0) {
-        const u64* hin = xb[B_HOUT] + (size_t)((gi - 1) & 1) * TP * HWORDS;
-        fail = load_rows_poll<ModT>(p, c, hin, tag - 1u, hv, ST_QKV) != 0;
-        if (__syncthreads_or(fail)) goto drain;
+      const int q_sa = s * per + 3 * l;
+      for (int st = 0; st < 9; ++st) {
+        int rc = 0;
+        if (st == 8) {
+          if (l + 1 < L) break;
+          rc = stage_tail<ModT>(p, c, s);
+        } else if (st == 0 || st == 3 || st == 6) {
+          rc = stage_norm_gemm<ModT>(p, c, st / 3, gi, l, q_sa + st / 3);
+        } else if (st == 1 || st == 4) {
+          rc = stage_attention(p, c, st == 1, gi, l);
+        } else {  // st 2, 5, 7
+          const int which = st == 2 ? 0 : (st == 5 ? 1 : 2);
+          rc = stage_words_gemm<ModT>(p, c, which, gi, q_sa + which);
+        }
+        if (rc) goto drain;
+        stage_done(p, c);
       }
-      stage_adarms<ModT>(p, c, hv, m_sa);
-      fail = !wait_bar(p, c, S_QKV);
-      if (__syncthreads_or(fail)) goto drain;
-      consumed(c, S_QKV);
-      mma_from_x(p, c, c.slot[S_QKV], 1, c.R_qkv);
-      __syncthreads();
-      if (c.tid == 0 && gi + 1 < total) issue_slot(p, c, S_QKV, (gi + 1) % L);
-      if (!(p.drop_stage == ST_QKV && c.cta == 0 && gi == 0))
-        epi_plain(p, c, c.R_qkv, c.r0_qkv, xb[B_QKV] + (size_t)par * TP * QKVWORDS, QKVWORDS, tag);
-      c.stages++;
-
-      // 2. self-attention, one (head, row) unit per CTA
-      for (int u = c.cta; u < NH * p.T; u += c.G) {
-        fail = attention_unit<true>(p, c, l, u % NH, u / NH, xb[B_QKV] + (size_t)par * TP * QKVWORDS,
-                                    xb[B_Y] + (size_t)par * TP * HWORDS, tag) != 0;
-        if (__syncthreads_or(fail)) goto drain;
-      }
-      c.stages++;
-
-      // 3. h2 = bf16(h + bf16(y @ Wo^T) * gate_sa)
-      __syncthreads();
-      fail = !wait_bar(p, c, S_O);
-      if (__syncthreads_or(fail)) goto drain;
-      consumed(c, S_O);
-      fail = mma_from_words(p, c, c.slot[S_O], c.R_h, H, xb[B_Y] + (size_t)par * TP * HWORDS, tag, ST_O) != 0;
-      if (__syncthreads_or(fail)) goto drain;
-      if (c.tid == 0 && gi + 1 < total) issue_slot(p, c, S_O, (gi + 1) % L);
-      epi_gated<ModT>(p, c, m_sa + 2 * H, xb[B_H2] + (size_t)par * TP * HWORDS, tag, nullptr);
-      c.stages++;
-      __syncthreads();
-
-      // 4. CA query = bf16(AdaRMS(h2; ca) @ Wqca^T)
-      fail = load_rows_poll<ModT>(p, c, xb[B_H2] + (size_t)par * TP * HWORDS, tag, hv, ST_CAQ) != 0;
-      if (__syncthreads_or(fail)) goto drain;
-      stage_adarms<ModT>(p, c, hv, m_ca);
-      fail = !wait_bar(p, c, S_QCA);
-      if (__syncthreads_or(fail)) goto drain;
-      consumed(c, S_QCA);
-      mma_from_x(p, c, c.slot[S_QCA], 1, c.R_h);
-      __syncthreads();
-      if (c.tid == 0 && gi + 1 < total) issue_slot(p, c, S_QCA, (gi + 1) % L);
-      epi_plain(p, c, c.R_h, c.c0, xb[B_QCA] + (size_t)par * TP * HWORDS, HWORDS, tag);
-      c.stages++;
-
-      // 5. cross-attention
-      for (int u = c.cta; u < NH * p.T; u += c.G) {
-        fail = attention_unit<false>(p, c, l, u % NH, u / NH, xb[B_QCA] + (size_t)par * TP * HWORDS,
-                                     xb[B_YCA] + (size_t)par * TP * HWORDS, tag) != 0;
-        if (__syncthreads_or(fail)) goto drain;
-      }
-      c.stages++;
-
-      // 6. h3 = bf16(h2 + bf16(y_ca @ Woca^T) * gate_ca)
-      __syncthreads();
-      fail = !wait_bar(p, c, S_OCA);
-      if (__syncthreads_or(fail)) goto drain;
-      consumed(c, S_OCA);
-      fail = mma_from_words(p, c, c.slot[S_OCA], c.R_h, H, xb[B_YCA] + (size_t)par * TP * HWORDS, tag, ST_OCA) != 0;
-      if (__syncthreads_or(fail)) goto drain;
-      if (c.tid == 0 && gi + 1 < total) issue_slot(p, c, S_OCA, (gi + 1) % L);
-      epi_gated<ModT>(p, c, m_ca + 2 * H, xb[B_H3] + (size_t)par * TP * HWORDS, tag, nullptr);
-      c.stages++;
-      __syncthreads();
-
-      // 7. g = bf16(silu(gate) * up) of AdaRMS(h3; mlp)
-      fail = load_rows_poll<ModT>(p, c, xb[B_H3] + (size_t)par * TP * HWORDS, tag, hv, ST_GU) != 0;
-      if (__syncthreads_or(fail)) goto drain;
-      stage_adarms<ModT>(p, c, hv, m_mlp);
-      fail = !wait_bar(p, c, S_GU);
-      if (__syncthreads_or(fail)) goto drain;
-      consumed(c, S_GU);
-      mma_from_x(p, c, c.slot[S_GU], 2, c.R_gu);
-      __syncthreads();
-      if (c.tid == 0) {
-        if (gi + 1 < total) issue_slot(p, c, S_GU, (gi + 1) % L);
-        if (l == L - 1 && s + 1 < p.n_steps) issue_tail(p, c);  // X is dead until the tail
-      }
-      epi_gu(p, c, xb[B_G] + (size_t)par * TP * (p.I >> 1), tag);
-      c.stages++;
-
-      // 8. h = bf16(h3 + bf16(g @ Wd^T) * gate_mlp)
-      __syncthreads();
-      fail = !wait_bar(p, c, S_D);
-      if (__syncthreads_or(fail)) goto drain;
-      consumed(c, S_D);
-      fail = mma_from_words(p, c, c.slot[S_D], c.R_h, p.I, xb[B_G] + (size_t)par * TP * (p.I >> 1), tag, ST_DOWN) != 0;
-      if (__syncthreads_or(fail)) goto drain;
-      if (c.tid == 0 && gi + 1 < total) issue_slot(p, c, S_D, (gi + 1) % L);
-      epi_gated<ModT>(p, c, m_mlp + 2 * H, xb[B_HOUT] + (size_t)par * TP * HWORDS, tag,
-                      p.trace_h ? p.trace_h + (size_t)gi * p.T * H : nullptr);
-      c.stages++;
-      __syncthreads();
-    }
-    // Euler step tail: final AdaRMS, velocity, x update, next step's h0.
-    {
-      const int gl = s * L + L - 1;
-      const u64* hrows = p.xb[B_HOUT] + (size_t)(gl & 1) * TP * HWORDS;
-      const ModT* modf = mrow + (size_t)9 * L * H;
-      const bool last = s + 1 == p.n_steps;
-      if (!last) {
-        fail = !wait_bar(p, c, NSLOT);
-        if (__syncthreads_or(fail)) goto drain;
-        consumed(c, NSLOT);
-      }
-      fail = step_tail<ModT>(p, c, last ? 2 : 1, modf, hrows, c.tag0 + (uint32_t)gl, hv) != 0;
-      if (__syncthreads_or(fail)) goto drain;
-      c.stages++;
     }
   }
 
 drain:
   // Normal exit: nothing is in flight. After a failed wait: drain every issued bulk copy (bounded).
+  __syncthreads();
   if (c.tid == 0) {
-    for (int b = 0; b < NSLOT + 1; ++b) {
-      while (c.cnt[NSLOT + 1 + b] < c.cnt[b]) {
-        const uint32_t parity = (uint32_t)(c.cnt[NSLOT + 1 + b] & 1);
-        uint64_t t0 = globaltimer();
+    int* cnt = cCnt(p, c);
+    for (int b = 0; b < NBAR; ++b) {
+      while (cnt[NBAR + b] < cnt[b]) {
+        const uint32_t parity = (uint32_t)(cnt[NBAR + b] & 1);
+        const uint64_t t0 = globaltimer();
         bool ok = false;
-        while (!(ok = mbar_try_wait(&c.bar[b], parity))) {
+        while (!(ok = mbar_try_wait(&cBar(p, c)[b], parity))) {
           if (globaltimer() - t0 > p.timeout_ns) break;
         }
-        c.cnt[NSLOT + 1 + b] += 1;
+        cnt[NBAR + b] += 1;
         if (!ok) break;
       }
     }
@@ -1058,7 +1141,7 @@ struct mkx_handle {
   int G;
   int smem;
   Params base;     // weight / scratch pointers and smem layout; per-call fields filled in mkx_run
-  void* alloc[16];
+  void* alloc[24];
   int nalloc;
   unsigned long long timeout_ns;
   int drop_stage;
@@ -1089,7 +1172,7 @@ static void* halloc(mkx_handle* h, size_t bytes, cudaError_t* err) {
 
 struct Layout {
   int s_slot[NSLOT];
-  int s_u, s_p, s_x, s_res, s_red, s_bar, s_cnt, total;
+  int s_x, s_p, s_mods, s_xs, s_res, s_red, s_bar, s_cnt, total;
   int max_rows_qkv, max_rows_h, max_rows_gu;
 };
 
@@ -1127,14 +1210,14 @@ static Layout make_layout(int I, int G) {
   ly.s_slot[S_OCA] = take(ly.max_rows_h * H * 2);
   ly.s_slot[S_GU] = take(ly.max_rows_gu * H * 4);
   ly.s_slot[S_D] = take(ly.max_rows_h * I * 2);
-  const int xbytes = TP * XS * 2;
-  ly.s_u = take(xbytes > TAIL_BYTES ? xbytes : TAIL_BYTES);
-  ly.s_p = take(NW * 256 * 4 > (32 * 64 + 32) * 4 ? NW * 256 * 4 : (32 * 64 + 32) * 4);
-  ly.s_x = take(TP * 32 * 4);
+  ly.s_x = take(TP * XS * 2);
+  ly.s_p = take((32 * 64 + 32) * 4 > NW * 256 * 4 ? (32 * 64 + 32) * 4 : NW * 256 * 4);
+  ly.s_mods = take(2 * 3 * H * 4);  // sized for fp32 modulations
+  ly.s_xs = take(TP * 32 * 4);
   ly.s_res = take(TP * RESW * 4);
-  ly.s_red = take(64 * 4);
-  ly.s_bar = take((NSLOT + 1) * 8);
-  ly.s_cnt = take(2 * (NSLOT + 1) * 4);
+  ly.s_red = take((16 + NW * AO) * 4);
+  ly.s_bar = take(NBAR * 8);
+  ly.s_cnt = take(2 * NBAR * 4);
   ly.total = off;
   return ly;
 }
@@ -1160,10 +1243,11 @@ extern "C" mkx_status mkx_create(const mkx_dims* dims, const mkx_weights* w, int
   MKX_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
   MKX_CUDA(cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
   const int G = d.grid > 0 ? d.grid : sms;
-  if (G < d.A || G > H / 2 || G > sms) return MKX_ERR_RESOURCES;
+  if (G < d.A || G < TP || G > H / 2 || G > sms) return MKX_ERR_RESOURCES;
   if (min_part(d.I / 2, G) < 1) return MKX_ERR_RESOURCES;
   const Layout ly = make_layout(d.I, G);
-  if (ly.max_rows_qkv > 128 || ly.max_rows_h > RESW || ly.max_rows_gu > 64) return MKX_ERR_RESOURCES;
+  // one epilogue element (column pair, action row) per thread
+  if (ly.max_rows_qkv / 2 * TP > NT || ly.max_rows_h > RESW || ly.max_rows_gu / 2 * TP > NT) return MKX_ERR_RESOURCES;
   if (ly.total > smem_optin) return MKX_ERR_RESOURCES;
 
   mkx_handle* h = new (std::nothrow) mkx_handle();
@@ -1185,9 +1269,9 @@ extern "C" mkx_status mkx_create(const mkx_dims* dims, const mkx_weights* w, int
     if (err != cudaSuccess) { mkx_destroy(h); return cuda_fail(err, "cudaMalloc(weights)"); }
   }
   float* nrm = (float*)halloc(h, (size_t)3 * L * HD * 4, &err);
-  float* tailw = err == cudaSuccess ? (float*)halloc(h, TAIL_BYTES, &err) : nullptr;
+  float* tailw = err == cudaSuccess ? (float*)halloc(h, TAIL_FLOATS * 4, &err) : nullptr;
   float* wout = err == cudaSuccess ? (float*)halloc(h, (size_t)A * H * 4, &err) : nullptr;
-  const int rw[NBUF] = {QKVWORDS, HWORDS, HWORDS, HWORDS, HWORDS, HWORDS, I / 2, HWORDS};
+  const int rw[NBUF] = {QKVWORDS, HWORDS, HWORDS, HWORDS, HWORDS, HWORDS, I / 2, HWORDS, XWORDS};
   size_t xwords = 0;
   for (int b = 0; b < NBUF; ++b) xwords += (size_t)2 * TP * rw[b];
   u64* xbase = err == cudaSuccess ? (u64*)halloc(h, xwords * 8, &err) : nullptr;
@@ -1204,12 +1288,11 @@ extern "C" mkx_status mkx_create(const mkx_dims* dims, const mkx_weights* w, int
   pack_kernel<<<blocks, 256, 0, st>>>(w->wg, w->wu, wp[S_GU], L, I, H, G, 2);
   pack_kernel<<<blocks, 256, 0, st>>>(w->wd, nullptr, wp[S_D], L, H, I, G, 1);
   norm_kernel<<<(3 * L * HD + 255) / 256, 256, 0, st>>>(w->qn, w->kn, w->qcan, nrm, L);
-  // tail weights: wout rows 0..7 | win rows 0..7 | bin | bout (padded to 32)
-  cudaMemsetAsync(tailw, 0, TAIL_BYTES, st);
-  cudaMemcpyAsync(tailw, w->wout, (size_t)AO * H * 4, cudaMemcpyDeviceToDevice, st);
-  cudaMemcpyAsync(tailw + AO * H, w->win, (size_t)AO * H * 4, cudaMemcpyDeviceToDevice, st);
-  cudaMemcpyAsync(tailw + 2 * AO * H, w->bin, (size_t)H * 4, cudaMemcpyDeviceToDevice, st);
-  cudaMemcpyAsync(tailw + 2 * AO * H + H, w->bout, (size_t)A * 4, cudaMemcpyDeviceToDevice, st);
+  // tail weights: win rows 0..7 | bin | bout (padded to 32); wout keeps all A rows
+  cudaMemsetAsync(tailw, 0, TAIL_FLOATS * 4, st);
+  cudaMemcpyAsync(tailw, w->win, (size_t)AO * H * 4, cudaMemcpyDeviceToDevice, st);
+  cudaMemcpyAsync(tailw + AO * H, w->bin, (size_t)H * 4, cudaMemcpyDeviceToDevice, st);
+  cudaMemcpyAsync(tailw + AO * H + H, w->bout, (size_t)A * 4, cudaMemcpyDeviceToDevice, st);
   cudaMemcpyAsync(wout, w->wout, (size_t)A * H * 4, cudaMemcpyDeviceToDevice, st);
   cudaMemsetAsync(xbase, 0, xwords * 8, st);
   cudaMemsetAsync(status, 0, 64, st);
@@ -1222,7 +1305,9 @@ extern "C" mkx_status mkx_create(const mkx_dims* dims, const mkx_weights* w, int
     mkx_destroy(h);
     return cuda_fail(err != cudaSuccess ? err : e2, "pack");
   }
-  if ((err = set_smem_attr<uint16_t>(ly.total)) != cudaSuccess || (err = set_smem_attr<float>(ly.total)) != cudaSuccess) {
+  // The attribute belongs to the kernel function, shared by every handle in the process: always
+  // allow the device maximum so a smaller handle never lowers what a larger one needs.
+  if ((err = set_smem_attr<uint16_t>(smem_optin)) != cudaSuccess || (err = set_smem_attr<float>(smem_optin)) != cudaSuccess) {
     mkx_destroy(h);
     return cuda_fail(err, "cudaFuncSetAttribute");
   }
@@ -1250,7 +1335,7 @@ extern "C" mkx_status mkx_create(const mkx_dims* dims, const mkx_weights* w, int
   p.qk_eps = d.qk_eps;
   p.sm_scale = 1.0f / sqrtf((float)HD);
   for (int s = 0; s < NSLOT; ++s) p.s_slot[s] = ly.s_slot[s];
-  p.s_u = ly.s_u; p.s_p = ly.s_p; p.s_x = ly.s_x; p.s_res = ly.s_res;
+  p.s_x = ly.s_x; p.s_p = ly.s_p; p.s_mods = ly.s_mods; p.s_xs = ly.s_xs; p.s_res = ly.s_res;
   p.s_red = ly.s_red; p.s_bar = ly.s_bar; p.s_cnt = ly.s_cnt;
   *out = h;
   return MKX_OK;
@@ -1269,7 +1354,7 @@ extern "C" mkx_status mkx_run(mkx_handle* h, const mkx_step_inputs* in, cudaStre
   if (in->mem_row_stride < H || in->mem_row_stride % 8 || in->ca_row_stride < H || in->ca_row_stride % 8)
     return MKX_ERR_INVALID_ARG;
   if (!aligned16(in->sa_cos) || !aligned16(in->sa_sin) || !aligned16(in->ca_cos) || !aligned16(in->ca_sin) ||
-      ((uintptr_t)in->mods & 7u))
+      !aligned16(in->mods))
     return MKX_ERR_INVALID_ARG;
   for (int l = 0; l < d.L; ++l) {
     if (!in->memk[l] || !in->memv[l] || !in->kca[l] || !in->vca[l]) return MKX_ERR_INVALID_ARG;
@@ -1298,6 +1383,7 @@ extern "C" mkx_status mkx_run(mkx_handle* h, const mkx_step_inputs* in, cudaStre
   p.ca_cos = in->ca_cos;
   p.ca_sin = in->ca_sin;
   p.trace_h = in->trace_h;
+  p.prof = in->prof;
   p.timeout_ns = h->timeout_ns;
   p.drop_stage = h->drop_stage;
   p.T = in->T;

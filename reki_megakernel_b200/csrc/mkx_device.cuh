@@ -15,11 +15,12 @@ __device__ __forceinline__ uint64_t globaltimer() {
 }
 
 // ---- exchange words: {payload u32 (low), tag u32 (high)}, 8-byte single-copy-atomic accesses ----
+// Relaxed, gpu-scope (morally strong, so each aligned 8-byte element is single-copy atomic).
 __device__ __forceinline__ void ld_volatile_v2(const u64* p, u64& a, u64& b) {
-  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 __device__ __forceinline__ void st_volatile(u64* p, u64 v) {
-  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 __device__ __forceinline__ int ld_volatile_i32(const int* p) {
   int v;
@@ -97,6 +98,35 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 // Orders this thread's earlier generic-proxy shared-memory accesses before later async-proxy ones.
 __device__ __forceinline__ void fence_proxy_async() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Read-only global loads pinned where they are written: volatile asm keeps them ahead of the
+// (volatile) exchange polls that follow, so their latency overlaps the wait instead of being paid
+// after it. For kernel-lifetime read-only data only.
+__device__ __forceinline__ uint2 ldg_u2_pin(const void* p) {
+  uint2 v;
+  asm volatile("ld.global.nc.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ float4 ldg_f4_pin(const void* p) {
+  float4 v;
+  asm volatile("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ float2 ldg_f2_pin(const void* p) {
+  float2 v;
+  asm volatile("ld.global.nc.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ float ldg_f1_pin(const void* p) {
+  float v;
+  asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ u64 ld_volatile(const u64* p) {
+  u64 v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
 }
 
 __device__ __forceinline__ uint2 lds64(const void* p) {

@@ -85,7 +85,7 @@ class ExpertMegakernel:
         return self._dt_cache[key]
 
     def run(self, x_t: torch.Tensor, mods: torch.Tensor, dt, past, action_dim: int,
-            trace: torch.Tensor | None = None) -> torch.Tensor:
+            trace: torch.Tensor | None = None, prof: torch.Tensor | None = None) -> torch.Tensor:
         """x_t: [1, T, A] fp32 after Euler step 1; mods: [N, MODW] (row 0 = step 1, used already);
         returns x_t after step N (padded dims as the reference: 0 + dt * v)."""
         step = past.register_step
@@ -138,6 +138,8 @@ class ExpertMegakernel:
         if mods.dtype not in (torch.bfloat16, torch.float32):
             mods = mods.float()
         mods = mods.contiguous()
+        if mods.data_ptr() % 16:  # the modulation rows are bulk-copied (TMA): 16-byte aligned source
+            mods = mods.clone()
         dt_t = self._dt_tensor(dt)
         out = torch.empty(T, self.A, dtype=torch.float32, device=self.device)
         if trace is not None:
@@ -156,6 +158,11 @@ class ExpertMegakernel:
         si.sa_cos, si.sa_sin, si.ca_cos, si.ca_sin = (t.data_ptr() for t in (sa_cos, sa_sin, ca_cos, ca_sin))
         si.T, si.n_steps, si.action_dim = T, n_steps, int(action_dim)
         si.trace_h = trace.data_ptr() if trace is not None else None
+        if prof is not None:
+            need = self.nprog * (1 + self.barriers(n_steps))
+            if prof.dtype != torch.int64 or prof.numel() < need or not prof.is_contiguous():
+                raise ValueError(f"prof must be a contiguous int64 tensor of >= {need} elements")
+            si.prof = prof.data_ptr()
         stream = torch.cuda.current_stream(self.device).cuda_stream
         _lib.check(self._lib.mkx_run(self._h, C.byref(si), C.c_void_p(stream)), "mkx_run")
         return out.reshape(1, T, self.A)

