@@ -134,6 +134,37 @@ mkx_status mkx_set_fault_injection(mkx_handle* h, int stage);
 /* Grid size actually used and dynamic shared memory bytes per CTA. */
 mkx_status mkx_launch_shape(const mkx_handle* h, int* grid, int* smem_bytes);
 
+/* Weights already in the kernel's packed layout, in device memory the caller owns. The layout
+ * depends on the grid size; reki_megakernel_b200/packing.py writes it from the stacked weights:
+ *   w[0..5]  bf16 QKV, O, CA-Q, CA-O, gate+up, down: each CTA's rows as [K/16][rows][16]
+ *   nrm      fp32 [3, L, HD]: 1 + q_norm, 1 + k_norm, 1 + ca q_norm
+ *   tailw    fp32 [8 * H + H + 32]: action_in_proj rows 0..7 (transposed), its bias, the out bias
+ *   wout     fp32 [A, H]: action_out_proj.weight */
+typedef struct {
+  const uint16_t* w[6];
+  const float* nrm;
+  const float* tailw;
+  const float* wout;
+} mkx_packed_weights;
+
+/* No counterpart in the reference: an extra entry point for callers that cannot allocate device
+ * memory themselves -- a runtime that hands every buffer out of one arena reserved at start-up, or
+ * a control loop that may not call cudaMalloc/cudaFree once it is running, because an allocation
+ * can block on the device and break the loop's timing. It runs one launch of the same kernel as
+ * mkx_run without a handle: the caller passes packed weights (mkx_packed_weights, packed for
+ * dims->grid; 0 = one CTA per SM), the step inputs and x_out, all in memory it owns, plus an
+ * optional device int err_out that receives the launch's error word (0 when every wait finished).
+ * The kernel's scratch -- the exchange buffers and status words -- is a file-scope static device
+ * array of 1,286,176 bytes, which every GPU that loads this library keeps until the process exits;
+ * it holds I <= 3072 and T <= 16, and larger sizes return MKX_ERR_UNSUPPORTED with a message in
+ * mkx_last_cuda_error(). Nothing in this call allocates. The first call on a device looks up the
+ * array's device address and raises the kernel's shared-memory limit, so make that first call
+ * before any stream capture. All calls share the one array and it keeps the last call's contents
+ * (the error word and stage counter are cleared on the stream before each launch): two calls
+ * whose launches overlap on the GPU race and corrupt each other. */
+mkx_status mkx_run_static(const mkx_dims* dims, const mkx_packed_weights* w, const mkx_step_inputs* in,
+                          int* err_out, cudaStream_t stream);
+
 /* Last CUDA error string seen by the library (thread-local, static storage). */
 const char* mkx_last_cuda_error(void);
 

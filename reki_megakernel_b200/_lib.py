@@ -40,6 +40,10 @@ class StepInputs(C.Structure):
                 ("T", C.c_int), ("n_steps", C.c_int), ("action_dim", C.c_int), ("trace_h", P), ("prof", P)]
 
 
+class PackedWeights(C.Structure):
+    _fields_ = [("w", P * 6), ("nrm", P), ("tailw", P), ("wout", P)]
+
+
 SIGNATURES = {
     "mkx_create": (C.c_int, [C.POINTER(Dims), C.POINTER(Weights), C.c_int, C.POINTER(P)]),
     "mkx_run": (C.c_int, [P, C.POINTER(StepInputs), P]),
@@ -49,6 +53,7 @@ SIGNATURES = {
     "mkx_set_timeout_ns": (C.c_int, [P, C.c_ulonglong]),
     "mkx_set_fault_injection": (C.c_int, [P, C.c_int]),
     "mkx_launch_shape": (C.c_int, [P, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+    "mkx_run_static": (C.c_int, [C.POINTER(Dims), C.POINTER(PackedWeights), C.POINTER(StepInputs), P, P]),
     "mkx_last_cuda_error": (C.c_char_p, []),
     "mkx_destroy": (None, [P]),
 }

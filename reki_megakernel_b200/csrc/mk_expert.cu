@@ -1462,3 +1462,162 @@ extern "C" void mkx_destroy(mkx_handle* h) {
   for (int i = 0; i < h->nalloc; ++i) cudaFree(h->alloc[i]);
   delete h;
 }
+
+// =============================================================================================
+// mkx_run_static: the same kernel for callers that cannot allocate. Its scratch lives in a
+// file-scope device array instead of handle memory; nothing below allocates.
+#include <mutex>
+
+namespace mkx {
+constexpr int STATIC_MAX_I = 3072;
+// exchange words of every buffer, both parities, TP rows, at the largest I; then 8 status ints
+constexpr size_t STATIC_XWORDS = (size_t)2 * TP * (QKVWORDS + 6 * HWORDS + STATIC_MAX_I / 2 + XWORDS);
+constexpr size_t STATIC_WORDS = STATIC_XWORDS + 4;  // 1,286,176 bytes
+static __device__ __align__(256) u64 g_static_scratch[STATIC_WORDS];
+}  // namespace mkx
+
+namespace {
+struct StaticDevice {
+  bool ready = false;
+  u64* scratch = nullptr;  // device address of g_static_scratch on this device
+  int sms = 0, smem_optin = 0;
+};
+StaticDevice g_static_dev[64];
+std::mutex g_static_mu;
+
+mkx_status static_fail(const char* msg, mkx_status st) {
+  snprintf(g_cuda_err, sizeof(g_cuda_err), "mkx_run_static: %s", msg);
+  return st;
+}
+
+// Once per device, with that device current: the scratch array's device address (the host-side
+// name g_static_scratch is only a stand-in) and the kernel's shared-memory limit.
+mkx_status static_setup(int dev, StaticDevice** out) {
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  StaticDevice& sd = g_static_dev[dev];
+  if (!sd.ready) {
+    void* ptr = nullptr;
+    MKX_CUDA(cudaGetSymbolAddress(&ptr, g_static_scratch));
+    MKX_CUDA(cudaDeviceGetAttribute(&sd.sms, cudaDevAttrMultiProcessorCount, dev));
+    MKX_CUDA(cudaDeviceGetAttribute(&sd.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    MKX_CUDA(set_smem_attr<uint16_t>(sd.smem_optin));
+    MKX_CUDA(set_smem_attr<float>(sd.smem_optin));
+    sd.scratch = static_cast<u64*>(ptr);
+    sd.ready = true;
+  }
+  *out = &sd;
+  return MKX_OK;
+}
+}  // namespace
+
+extern "C" mkx_status mkx_run_static(const mkx_dims* dims, const mkx_packed_weights* w, const mkx_step_inputs* in,
+                                     int* err_out, cudaStream_t stream) {
+  if (!dims || !w || !in) return MKX_ERR_INVALID_ARG;
+  const mkx_dims d = *dims;
+  if (d.H != H || d.NH != NH || d.HD != HD || d.L < 1 || d.L > MKX_MAX_LAYERS || d.I < 128 || d.I % 128 != 0 ||
+      d.A < AO || d.A > 32)
+    return static_fail("unsupported expert geometry", MKX_ERR_UNSUPPORTED);
+  if (d.I > STATIC_MAX_I) return static_fail("I exceeds the static scratch maximum of 3072", MKX_ERR_UNSUPPORTED);
+  if (in->T < 1 || in->T > TP) return static_fail("T exceeds the static scratch maximum of 16 rows", MKX_ERR_UNSUPPORTED);
+  if (in->n_steps < 1 || in->n_steps * d.L >= MAX_STEP_TAGS - 1 || in->action_dim < 1 || in->action_dim > AO)
+    return MKX_ERR_INVALID_ARG;
+  for (int s = 0; s < NSLOT; ++s)
+    if (!w->w[s] || !aligned16(w->w[s])) return MKX_ERR_INVALID_ARG;
+  if (!w->nrm || !w->tailw || !w->wout || !aligned16(w->tailw) || !aligned16(w->wout)) return MKX_ERR_INVALID_ARG;
+  if (!in->x_in || !in->x_out || !in->mods || !in->dt || !in->cu_kv || !in->cu_src || !in->sa_cos || !in->sa_sin ||
+      !in->ca_cos || !in->ca_sin)
+    return MKX_ERR_INVALID_ARG;
+  if (in->mem_rows < 1 || in->mem_rows > 32 * MAXK || in->ca_rows < 1) return MKX_ERR_UNSUPPORTED;
+  if (in->mem_row_stride < H || in->mem_row_stride % 8 || in->ca_row_stride < H || in->ca_row_stride % 8)
+    return MKX_ERR_INVALID_ARG;
+  if (!aligned16(in->sa_cos) || !aligned16(in->sa_sin) || !aligned16(in->ca_cos) || !aligned16(in->ca_sin) ||
+      !aligned16(in->mods))
+    return MKX_ERR_INVALID_ARG;
+  for (int l = 0; l < d.L; ++l) {
+    if (!in->memk[l] || !in->memv[l] || !in->kca[l] || !in->vca[l]) return MKX_ERR_INVALID_ARG;
+    if (((uintptr_t)in->memk[l] | (uintptr_t)in->memv[l] | (uintptr_t)in->kca[l] | (uintptr_t)in->vca[l]) & 7u)
+      return MKX_ERR_INVALID_ARG;
+  }
+  int dev = 0;
+  MKX_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return MKX_ERR_UNSUPPORTED;
+  StaticDevice* sd = nullptr;
+  const mkx_status st = static_setup(dev, &sd);
+  if (st != MKX_OK) return st;
+  const int G = d.grid > 0 ? d.grid : sd->sms;
+  if (G < d.A || G < TP || G > H / 2 || G > sd->sms || min_part(d.I / 2, G) < 1) return MKX_ERR_RESOURCES;
+  const Layout ly = make_layout(d.I, G);
+  if (ly.max_rows_qkv / 2 * TP > NT || ly.max_rows_h > RESW || ly.max_rows_gu / 2 * TP > NT ||
+      ly.total > sd->smem_optin)
+    return MKX_ERR_RESOURCES;
+
+  Params p;
+  memset(&p, 0, sizeof(p));
+  for (int s = 0; s < NSLOT; ++s) p.w[s] = w->w[s];
+  p.nrm = w->nrm;
+  p.tailw = w->tailw;
+  p.wout = w->wout;
+  const int rw[NBUF] = {QKVWORDS, HWORDS, HWORDS, HWORDS, HWORDS, HWORDS, d.I / 2, HWORDS, XWORDS};
+  u64* xp = sd->scratch;
+  for (int b = 0; b < NBUF; ++b) {
+    p.xb[b] = xp;
+    xp += (size_t)2 * TP * rw[b];
+  }
+  p.status = reinterpret_cast<int*>(sd->scratch + STATIC_XWORDS);  // [0] error, [1] sequence, [2..3] stages
+  p.L = d.L;
+  p.I = d.I;
+  p.A = d.A;
+  p.eps = d.eps;
+  p.qk_eps = d.qk_eps;
+  p.sm_scale = 1.0f / sqrtf((float)HD);
+  for (int s = 0; s < NSLOT; ++s) p.s_slot[s] = ly.s_slot[s];
+  p.s_x = ly.s_x; p.s_p = ly.s_p; p.s_mods = ly.s_mods; p.s_xs = ly.s_xs; p.s_res = ly.s_res;
+  p.s_red = ly.s_red; p.s_bar = ly.s_bar; p.s_cnt = ly.s_cnt;
+  p.x_in = in->x_in;
+  p.x_out = in->x_out;
+  p.mods = in->mods;
+  p.dt = in->dt;
+  for (int l = 0; l < d.L; ++l) {
+    p.memk[l] = in->memk[l];
+    p.memv[l] = in->memv[l];
+    p.kca[l] = in->kca[l];
+    p.vca[l] = in->vca[l];
+  }
+  p.mem_rows = in->mem_rows;
+  p.mem_row_stride = in->mem_row_stride;
+  p.ca_row_stride = in->ca_row_stride;
+  p.ca_rows = in->ca_rows;
+  p.cu_kv = in->cu_kv;
+  p.cu_src = in->cu_src;
+  p.sa_cos = in->sa_cos;
+  p.sa_sin = in->sa_sin;
+  p.ca_cos = in->ca_cos;
+  p.ca_sin = in->ca_sin;
+  p.trace_h = in->trace_h;
+  p.prof = in->prof;
+  p.timeout_ns = 2000000000ull;
+  p.drop_stage = 0;
+  p.T = in->T;
+  p.adim = in->action_dim;
+  p.n_steps = in->n_steps;
+
+  // The array keeps the previous call's contents: the error word and the stage counter must start
+  // at zero (the launch sequence number in between must not: it keeps tags from matching old words).
+  MKX_CUDA(cudaMemsetAsync(p.status, 0, sizeof(int), stream));
+  MKX_CUDA(cudaMemsetAsync(p.status + 2, 0, 2 * sizeof(int), stream));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(G);
+  cfg.blockDim = dim3(NT);
+  cfg.dynamicSmemBytes = ly.total;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = in->mods_fp32 ? cudaLaunchKernelEx(&cfg, expert_kernel<float>, p)
+                                : cudaLaunchKernelEx(&cfg, expert_kernel<uint16_t>, p);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(expert_kernel, static scratch)");
+  if (err_out) MKX_CUDA(cudaMemcpyAsync(err_out, p.status, sizeof(int), cudaMemcpyDeviceToDevice, stream));
+  return MKX_OK;
+}

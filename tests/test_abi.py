@@ -53,7 +53,8 @@ def _c_layout(struct: str, fields):
     return {k: int(v) for k, v in (line.split() for line in out.splitlines())}
 
 
-@pytest.mark.parametrize("struct,cls", [("mkx_dims", "Dims"), ("mkx_weights", "Weights"), ("mkx_step_inputs", "StepInputs")])
+@pytest.mark.parametrize("struct,cls", [("mkx_dims", "Dims"), ("mkx_weights", "Weights"), ("mkx_step_inputs", "StepInputs"),
+                                        ("mkx_packed_weights", "PackedWeights")])
 def test_struct_layout_matches_c(struct, cls):
     from reki_megakernel_b200 import _lib
     ct = getattr(_lib, cls)
