@@ -50,8 +50,12 @@ constexpr int XS = H + 8;                // shared X row stride (bf16 elements):
 constexpr int HWORDS = H / 2;            // exchange words per H-wide row
 constexpr int QKVWORDS = 3 * H / 2;
 constexpr int XWORDS = 32;               // exchange words per action-state row (fp32 payloads)
-constexpr int MAXK = 8;                  // keys per 8-lane group per attention chunk (x32 groups)
+constexpr int NG = NT / 8;               // attention: 8-lane key groups per CTA
+constexpr int MAXK = 8;                  // keys per group per attention chunk (NG * MAXK keys)
 constexpr int RESW = 8;                  // residual columns kept per CTA (o / ca-o / down rows)
+constexpr int SROW = NT / TP;            // staging threads per action row
+constexpr int SPAIRS = HWORDS / 2 / SROW; // 16-byte word pairs per staging thread
+constexpr int NCOL = (H + NT - 1) / NT;   // in-projection columns per thread
 constexpr int TAIL_FLOATS = AO * H + H + 32;   // win rows 0..7 | bin | bout (padded)
 constexpr int MAX_STEP_TAGS = 4096;      // tag = seq * 4096 + instance + 1
 
@@ -147,9 +151,25 @@ __device__ __forceinline__ void record_error(const Params& p, const Cta& c, int 
   atomicCAS(p.status, 0, (c.cta << 16) | (kind << 8) | stage);
 }
 
+// Sub-stage tracing, compiled only with -DMKX_SUBSTAGE_TRACE (a separate profiling build): thread 0
+// of CTAs 0 and 100 stamps %globaltimer at numbered points inside each stage, after the per-CTA
+// stage-end stamps of the prof buffer: [2][1 + stages][8].
+#ifdef MKX_SUBSTAGE_TRACE
+__device__ __forceinline__ void trace_point(const Params& p, const Cta& c, int pt) {
+  if (p.prof != nullptr && c.tid == 0 && (c.cta == 0 || c.cta == 100)) {
+    const size_t per_cta = 2 + (size_t)p.n_steps * (8 * p.L + 1);
+    p.prof[(size_t)c.G * per_cta + (c.cta == 0 ? 0 : per_cta * 8) + (size_t)c.stages * 8 + pt] = globaltimer();
+  }
+}
+#define MKX_TRACE(pt) trace_point(p, c, pt)
+#else
+#define MKX_TRACE(pt) ((void)0)
+#endif
+
 // Optional timeline: thread 0 of every CTA stamps %globaltimer at the launch start (index 0) and at
 // the end of every stage (index 1 + stage).
 __device__ __forceinline__ void stage_done(const Params& p, Cta& c) {
+  MKX_TRACE(7);
   c.stages++;
   if (p.prof != nullptr && c.tid == 0)
     p.prof[(size_t)c.cta * (2 + p.n_steps * (8 * p.L + 1)) + c.stages] = globaltimer();
@@ -280,24 +300,24 @@ __device__ __forceinline__ int fail_code(const Params& p, const Cta& c, int r, i
 }
 
 // ---------------------------------------------------------------------------------------------
-// AdaRMS staging: thread (n = tid / 16, part = tid % 16) owns 12 word pairs of action row n,
-// q = part + 16 j, i.e. columns {16kb + 2cc, +1} and {16kb + 2cc + 8, +9} with kb = q / 4, cc = q % 4.
+// AdaRMS staging: thread (n = tid / SROW, part = tid % SROW) owns SPAIRS word pairs of action row n,
+// q = part + SROW j, i.e. columns {16kb + 2cc, +1} and {16kb + 2cc + 8, +9} with kb = q / 4, cc = q % 4.
 __device__ __forceinline__ int col_a_of(int q) { return 16 * (q >> 2) + 2 * (q & 3); }
 
-// Polls action rows (row n of thread n = tid / 16) of an exchange buffer and writes the raw bf16
+// Polls action rows (row n of thread n = tid / SROW) of an exchange buffer and writes the raw bf16
 // values into X (natural layout). Returns nonzero on a failed wait (not CTA-uniform).
 __device__ int poll_rows_to_x(const Params& p, const Cta& c, const u64* rows, uint32_t tag, int stage) {
-  const int n = c.tid >> 4, part = c.tid & 15;
+  const int n = c.tid / SROW, part = c.tid % SROW;
   const u64* base = rows + (size_t)n * HWORDS + 2 * part;
-  auto addr = [base](int j) { return base + 32 * j; };
-  u64 w0[12], w1[12];
+  auto addr = [base](int j) { return base + 2 * SROW * j; };
+  u64 w0[SPAIRS], w1[SPAIRS];
   Waiter wt(p.status, p.timeout_ns);
-  issue_pairs<12>(addr, w0, w1, n < p.T ? 0xfffu : 0u, tag);
-  const int r = complete_pairs<12>(addr, w0, w1, tag, wt);
+  issue_pairs<SPAIRS>(addr, w0, w1, n < p.T ? (1u << SPAIRS) - 1u : 0u, tag);
+  const int r = complete_pairs<SPAIRS>(addr, w0, w1, tag, wt);
   char* xrow = cX(p, c) + (size_t)n * XS * 2;
 #pragma unroll
-  for (int j = 0; j < 12; ++j) {
-    const int ca = col_a_of(part + 16 * j);
+  for (int j = 0; j < SPAIRS; ++j) {
+    const int ca = col_a_of(part + SROW * j);
     *reinterpret_cast<uint32_t*>(xrow + ca * 2) = payload_of(w0[j]);
     *reinterpret_cast<uint32_t*>(xrow + (ca + 8) * 2) = payload_of(w1[j]);
   }
@@ -306,18 +326,18 @@ __device__ int poll_rows_to_x(const Params& p, const Cta& c, const u64* rows, ui
 
 // In place on X (raw h in, after a __syncthreads): a = bf16(h * rstd * (1 + scale) + shift), rows
 // >= T zero, and h kept at the CTA's residual columns (src/mk_expert.py:93-122). msc: [scale H |
-// shift H] in shared memory. Thread (n = tid / 16, part) owns the 48 columns of word pairs
-// part + 16 j of row n; loops are kept rolled to keep the routine small.
+// shift H] in shared memory. Thread (n = tid / SROW, part) owns the 4 SPAIRS columns of word pairs
+// part + SROW j of row n; loops are kept rolled to keep the routine small.
 template <typename ModT>
 __device__ void stage_adarms(const Params& p, Cta& c, const ModT* msc) {
-  const int n = c.tid >> 4, part = c.tid & 15;
+  const int n = c.tid / SROW, part = c.tid % SROW;
   const ModT* msh = msc + H;
   char* xrow = cX(p, c) + (size_t)n * XS * 2;
   const bool live = n < p.T;
   float ss = 0.f;
 #pragma unroll 2
-  for (int j = 0; j < 12; ++j) {
-    const int ca = col_a_of(part + 16 * j);
+  for (int j = 0; j < SPAIRS; ++j) {
+    const int ca = col_a_of(part + SROW * j);
     const uint32_t u = *reinterpret_cast<const uint32_t*>(xrow + ca * 2);
     const uint32_t v = *reinterpret_cast<const uint32_t*>(xrow + (ca + 8) * 2);
     const float a = bf_lo(u), b = bf_hi(u), d = bf_lo(v), e = bf_hi(v);
@@ -326,15 +346,13 @@ __device__ void stage_adarms(const Params& p, Cta& c, const ModT* msc) {
     ss = fmaf(d, d, ss);
     ss = fmaf(e, e, ss);
   }
-  ss += __shfl_xor_sync(0xffffffffu, ss, 8);
-  ss += __shfl_xor_sync(0xffffffffu, ss, 4);
-  ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-  ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+#pragma unroll
+  for (int o = SROW / 2; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   const float rstd = rsqrtf(ss / (float)H + p.eps);
   float* res = cRes(p, c) + n * RESW;
 #pragma unroll 1
-  for (int j = 0; j < 24; ++j) {  // 24 column pairs: (ca, ca+1) then (ca+8, ca+9) of word pair j / 2
-    const int col = col_a_of(part + 16 * (j >> 1)) + 8 * (j & 1);
+  for (int j = 0; j < 2 * SPAIRS; ++j) {  // column pairs (ca, ca+1) then (ca+8, ca+9) of word pair j / 2
+    const int col = col_a_of(part + SROW * (j >> 1)) + 8 * (j & 1);
     uint32_t* px = reinterpret_cast<uint32_t*>(xrow + col * 2);
     const uint32_t u = *px;
     const float h0 = bf_lo(u), h1 = bf_hi(u);
@@ -609,7 +627,7 @@ __device__ __forceinline__ int attention_unit(const Params& p, Cta& c, const boo
   auto load_chunk = [&](int base) {
 #pragma unroll
     for (int i = 0; i < MAXK; ++i) {
-      const int j = base + kg + 32 * i;
+      const int j = base + kg + NG * i;
       kA[i] = kB[i] = vA[i] = vB[i] = make_uint2(0u, 0u);
       if (j < nkeys) {
         const uint16_t* kr = Kb + (size_t)j * stride + h * HD + d0;
@@ -647,6 +665,7 @@ __device__ __forceinline__ int attention_unit(const Params& p, Cta& c, const boo
   const int rc = complete_pairs<6>(addr, w0, w1, tag, wt);
   fail_code(p, c, rc, SA ? ST_SA : ST_CA);
   if (__syncthreads_or(rc != 0)) return 1;
+  MKX_TRACE(1);
 
   Lane8 q;
   bf_words_to_lane(q, payload_of(w0[0]), payload_of(w1[0]), payload_of(w0[1]), payload_of(w1[1]));
@@ -663,19 +682,19 @@ __device__ __forceinline__ int attention_unit(const Params& p, Cta& c, const boo
 
   float m_run = -INFINITY, den = 0.f;
   float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  for (int base = kbeg; base < nkeys || (SA && base == kbeg); base += 32 * MAXK) {
+  for (int base = kbeg; base < nkeys || (SA && base == kbeg); base += NG * MAXK) {
     if (base != kbeg) load_chunk(base);
     float s[MAXK];
     float mloc = (SA && base == kbeg) ? s_own : -INFINITY;
 #pragma unroll
     for (int i = 0; i < MAXK; ++i) {
       // Key slot i holds a valid key for some groups only when nkeys - base is not a multiple of
-      // 32: the group-of-8 shuffles in dot8 must still run on every lane of the warp.
-      if (base + 32 * i >= nkeys) {  // uniform: no group has a key in this slot
+      // NG: the group-of-8 shuffles in dot8 must still run on every lane of the warp.
+      if (base + NG * i >= nkeys) {  // uniform: no group has a key in this slot
         s[i] = -INFINITY;
         continue;
       }
-      const int j = base + kg + 32 * i;
+      const int j = base + kg + NG * i;
       Lane8 k;
       bf_nat_to_lane(k, kA[i], kB[i]);
       const float dv = dot8(q, k) * p.sm_scale;
@@ -696,7 +715,7 @@ __device__ __forceinline__ int attention_unit(const Params& p, Cta& c, const boo
     }
 #pragma unroll
     for (int i = 0; i < MAXK; ++i) {
-      const int j = base + kg + 32 * i;
+      const int j = base + kg + NG * i;
       if (j < nkeys) {
         const float pe = __expf(s[i] - m_new);
         den += pe;
@@ -708,22 +727,34 @@ __device__ __forceinline__ int attention_unit(const Params& p, Cta& c, const boo
       }
     }
     m_run = m_new;
-    if (base + 32 * MAXK >= nkeys) break;
+    if (base + NG * MAXK >= nkeys) break;
   }
-  // Reduce the 32 groups: o in lane order per lane, den per group.
+  // Reduce the NG groups in two levels: o in lane order per lane, den per group.
+  MKX_TRACE(2);
   __syncthreads();
-  float* ro = cP(p, c);            // [32][64]
-  float* rd = cP(p, c) + 32 * 64;  // [32]
+  float* ro = cP(p, c);                  // [NG][64]
+  float* rd = ro + NG * 64;              // [NG]
+  float* r2 = rd + NG;                   // [4][64] second level
+  float* r2d = r2 + 4 * 64;              // [4]
 #pragma unroll
   for (int e = 0; e < 8; ++e) ro[kg * 64 + l8 * 8 + e] = o[e];
   if (l8 == 0) rd[kg] = den;
   __syncthreads();
-  if (c.tid < 64) {
+  if (c.tid < 256) {
+    const int slot = c.tid & 63, part = c.tid >> 6;
     float acc = 0.f, dsum = 0.f;
-    for (int gi = 0; gi < 32; ++gi) {
-      acc += ro[gi * 64 + c.tid];
+#pragma unroll 4
+    for (int gi = part * (NG / 4); gi < (part + 1) * (NG / 4); ++gi) {
+      acc += ro[gi * 64 + slot];
       dsum += rd[gi];
     }
+    r2[part * 64 + slot] = acc;
+    if (slot == 0) r2d[part] = dsum;
+  }
+  __syncthreads();
+  if (c.tid < 64) {
+    const float acc = (r2[c.tid] + r2[64 + c.tid]) + (r2[128 + c.tid] + r2[192 + c.tid]);
+    const float dsum = (r2d[0] + r2d[1]) + (r2d[2] + r2d[3]);
     const float val = acc / dsum;
     const float nxt = __shfl_down_sync(0xffffffffu, val, 1);
     if ((c.tid & 1) == 0)
@@ -842,26 +873,27 @@ __device__ int take_new_x(const Params& p, Cta& c, const u64* xrows, uint32_t xt
 }
 
 // In-projection h0 = bf16(xpad[:AO] @ Win[:AO] + bin) in fp32 (src/mk_expert.py:280-293) into X
-// (natural layout); thread t owns columns t, t + 256, t + 512, whose Win / bin values it loads
+// (natural layout); thread t owns columns t, t + NT, ... below H, whose Win / bin values it loads
 // up front.
-__device__ __forceinline__ void load_inproj(const Params& p, const Cta& c, float (&win)[3][AO], float (&bin)[3]) {
+__device__ __forceinline__ void load_inproj(const Params& p, const Cta& c, float (&win)[NCOL][AO], float (&bin)[NCOL]) {
 #pragma unroll
-  for (int k = 0; k < 3; ++k) {
-    const int col = c.tid + NT * k;
+  for (int k = 0; k < NCOL; ++k) {
+    const int col = min(c.tid + NT * k, H - 1);  // threads past H load a valid column and skip it
 #pragma unroll
     for (int a = 0; a < AO; ++a) win[k][a] = ldg_f1_pin(p.tailw + (size_t)a * H + col);
     bin[k] = ldg_f1_pin(p.tailw + AO * H + col);
   }
 }
 
-__device__ void in_proj_to_x(const Params& p, Cta& c, const float (&win)[3][AO], const float (&bin)[3]) {
+__device__ void in_proj_to_x(const Params& p, Cta& c, const float (&win)[NCOL][AO], const float (&bin)[NCOL]) {
 #pragma unroll 1
   for (int n = 0; n < TP; ++n) {
     float xp[AO];
 #pragma unroll
     for (int a = 0; a < AO; ++a) xp[a] = (a < p.adim && n < p.T) ? cXs(p, c)[n * 32 + a] : 0.f;
 #pragma unroll
-    for (int k = 0; k < 3; ++k) {
+    for (int k = 0; k < NCOL; ++k) {
+      if (c.tid + NT * k >= H) break;
       float acc = bin[k];
 #pragma unroll
       for (int a = 0; a < AO; ++a) acc = fmaf(xp[a], win[k][a], acc);
@@ -891,17 +923,21 @@ __device__ __forceinline__ int stage_norm_gemm(const Params& p, Cta& c, int whic
     const int fail = poll_rows_to_x(p, c, rows, which == 0 ? tag - 1u : tag, ST_QKV + 3 * which);
     if (__syncthreads_or(fail)) return 1;
   }
+  MKX_TRACE(0);
   int fail = !wait_bar(p, c, BAR_MODS + (q & 1));
   if (__syncthreads_or(fail)) return 1;
+  MKX_TRACE(1);
   consumed(p, c, BAR_MODS + (q & 1));
   stage_adarms<ModT>(p, c, mods_slot<ModT>(p, c, q));
   const int slot = which == 0 ? S_QKV : (which == 1 ? S_QCA : S_GU);
   fail = !wait_bar(p, c, slot);
   if (__syncthreads_or(fail)) return 1;
+  MKX_TRACE(2);
   consumed(p, c, slot);
   const int R = which == 0 ? c.R_qkv : (which == 1 ? c.R_h : c.R_gu);
   mma_from_x(p, c, cSlot(p, c, slot), which == 2 ? 2 : 1, R);
   __syncthreads();
+  MKX_TRACE(3);
   if (c.tid == ISSUER && gi + 1 < p.n_steps * p.L) issue_slot(p, c, slot, (gi + 1) % p.L);
   if (which == 2) {
     epi_gu(p, c, xb[B_G] + (size_t)par * TP * (p.I >> 1), tag);
@@ -929,8 +965,10 @@ __device__ __forceinline__ int stage_words_gemm(const Params& p, Cta& c, int whi
   int fail = !wait_bar(p, c, slot);
   if (__syncthreads_or(fail)) return 1;
   consumed(p, c, slot);
+  MKX_TRACE(0);
   fail = mma_from_words(p, c, cSlot(p, c, slot), c.R_h, K, rows, tag, ST_O + 3 * which);
   if (__syncthreads_or(fail)) return 1;
+  MKX_TRACE(1);
   if (c.tid == ISSUER && gi + 1 < p.n_steps * p.L) issue_slot(p, c, slot, (gi + 1) % p.L);
   u64* out = xb[which == 0 ? B_H2 : (which == 1 ? B_H3 : B_HOUT)] + (size_t)par * TP * HWORDS;
   epi_gated<ModT>(p, c, mods_slot<ModT>(p, c, q) + 2 * H, out, tag,
@@ -974,7 +1012,7 @@ __device__ __forceinline__ int stage_tail(const Params& p, Cta& c, int s) {
   __syncthreads();
   if (c.tid == ISSUER) issue_mods<ModT>(p, c, q_fin + 2);
   if (!last) {
-    float win[3][AO], bin[3];
+    float win[NCOL][AO], bin[NCOL];
     load_inproj(p, c, win, bin);  // in flight while the new action state is polled
     if (take_new_x(p, c, xrows, tl)) return 1;
     in_proj_to_x(p, c, win, bin);
@@ -1024,7 +1062,7 @@ __global__ void __launch_bounds__(NT, 1) expert_kernel(const __grid_constant__ P
   }
   {
     // FIRST tail: h0 from the action state after step 1, into X.
-    float win[3][AO], bin[3];
+    float win[NCOL][AO], bin[NCOL];
     load_inproj(p, c, win, bin);
     for (int e = c.tid; e < p.T * p.A; e += NT) cXs(p, c)[(e / p.A) * 32 + (e % p.A)] = __ldg(p.x_in + e);
     __syncthreads();
@@ -1211,7 +1249,8 @@ static Layout make_layout(int I, int G) {
   ly.s_slot[S_GU] = take(ly.max_rows_gu * H * 4);
   ly.s_slot[S_D] = take(ly.max_rows_h * I * 2);
   ly.s_x = take(TP * XS * 2);
-  ly.s_p = take((32 * 64 + 32) * 4 > NW * 256 * 4 ? (32 * 64 + 32) * 4 : NW * 256 * 4);
+  constexpr int attn_floats = NG * 64 + NG + 4 * 64 + 4;  // attention reductions, two levels
+  ly.s_p = take((attn_floats > NW * 256 ? attn_floats : NW * 256) * 4);
   ly.s_mods = take(2 * 3 * H * 4);  // sized for fp32 modulations
   ly.s_xs = take(TP * 32 * 4);
   ly.s_res = take(TP * RESW * 4);
@@ -1350,7 +1389,7 @@ extern "C" mkx_status mkx_run(mkx_handle* h, const mkx_step_inputs* in, cudaStre
   if (!in->x_in || !in->x_out || !in->mods || !in->dt || !in->cu_kv || !in->cu_src || !in->sa_cos || !in->sa_sin ||
       !in->ca_cos || !in->ca_sin)
     return MKX_ERR_INVALID_ARG;
-  if (in->mem_rows < 1 || in->mem_rows > 32 * MAXK || in->ca_rows < 1) return MKX_ERR_UNSUPPORTED;
+  if (in->mem_rows < 1 || in->mem_rows > NG * MAXK || in->ca_rows < 1) return MKX_ERR_UNSUPPORTED;
   if (in->mem_row_stride < H || in->mem_row_stride % 8 || in->ca_row_stride < H || in->ca_row_stride % 8)
     return MKX_ERR_INVALID_ARG;
   if (!aligned16(in->sa_cos) || !aligned16(in->sa_sin) || !aligned16(in->ca_cos) || !aligned16(in->ca_sin) ||
@@ -1527,7 +1566,7 @@ extern "C" mkx_status mkx_run_static(const mkx_dims* dims, const mkx_packed_weig
   if (!in->x_in || !in->x_out || !in->mods || !in->dt || !in->cu_kv || !in->cu_src || !in->sa_cos || !in->sa_sin ||
       !in->ca_cos || !in->ca_sin)
     return MKX_ERR_INVALID_ARG;
-  if (in->mem_rows < 1 || in->mem_rows > 32 * MAXK || in->ca_rows < 1) return MKX_ERR_UNSUPPORTED;
+  if (in->mem_rows < 1 || in->mem_rows > NG * MAXK || in->ca_rows < 1) return MKX_ERR_UNSUPPORTED;
   if (in->mem_row_stride < H || in->mem_row_stride % 8 || in->ca_row_stride < H || in->ca_row_stride % 8)
     return MKX_ERR_INVALID_ARG;
   if (!aligned16(in->sa_cos) || !aligned16(in->sa_sin) || !aligned16(in->ca_cos) || !aligned16(in->ca_sin) ||
