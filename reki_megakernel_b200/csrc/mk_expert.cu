@@ -304,42 +304,39 @@ __device__ __forceinline__ int fail_code(const Params& p, const Cta& c, int r, i
 // q = part + SROW j, i.e. columns {16kb + 2cc, +1} and {16kb + 2cc + 8, +9} with kb = q / 4, cc = q % 4.
 __device__ __forceinline__ int col_a_of(int q) { return 16 * (q >> 2) + 2 * (q & 3); }
 
-// Polls action rows (row n of thread n = tid / SROW) of an exchange buffer and writes the raw bf16
-// values into X (natural layout). Returns nonzero on a failed wait (not CTA-uniform).
-__device__ int poll_rows_to_x(const Params& p, const Cta& c, const u64* rows, uint32_t tag, int stage) {
-  const int n = c.tid / SROW, part = c.tid % SROW;
-  const u64* base = rows + (size_t)n * HWORDS + 2 * part;
-  auto addr = [base](int j) { return base + 2 * SROW * j; };
-  u64 w0[SPAIRS], w1[SPAIRS];
-  Waiter wt(p.status, p.timeout_ns);
-  issue_pairs<SPAIRS>(addr, w0, w1, n < p.T ? (1u << SPAIRS) - 1u : 0u, tag);
-  const int r = complete_pairs<SPAIRS>(addr, w0, w1, tag, wt);
-  char* xrow = cX(p, c) + (size_t)n * XS * 2;
-#pragma unroll
-  for (int j = 0; j < SPAIRS; ++j) {
-    const int ca = col_a_of(part + SROW * j);
-    *reinterpret_cast<uint32_t*>(xrow + ca * 2) = payload_of(w0[j]);
-    *reinterpret_cast<uint32_t*>(xrow + (ca + 8) * 2) = payload_of(w1[j]);
-  }
-  return fail_code(p, c, r, stage);
-}
-
-// In place on X (raw h in, after a __syncthreads): a = bf16(h * rstd * (1 + scale) + shift), rows
-// >= T zero, and h kept at the CTA's residual columns (src/mk_expert.py:93-122). msc: [scale H |
-// shift H] in shared memory. Thread (n = tid / SROW, part) owns the 4 SPAIRS columns of word pairs
-// part + SROW j of row n; loops are kept rolled to keep the routine small.
+// AdaRMS of action rows into X (src/mk_expert.py:93-122): a = bf16(h * rstd * (1 + scale) + shift),
+// rows >= T zero, and h kept at the CTA's residual columns. Thread (n = tid / SROW, part) owns the
+// 4 SPAIRS columns of word pairs part + SROW j of row n, held in registers from load to store: h
+// comes polled from an exchange buffer (`rows`), or, with rows == nullptr, from X itself (layer 0,
+// where the step tail left h0). The SROW threads of a row are one half-warp, so the row's sum of
+// squares is a shuffle reduction. msc: [scale H | shift H] in shared memory, already waited for.
+// Returns nonzero on a failed wait (not CTA-uniform).
 template <typename ModT>
-__device__ void stage_adarms(const Params& p, Cta& c, const ModT* msc) {
+__device__ int stage_rows_adarms(const Params& p, Cta& c, const u64* rows, uint32_t tag, int stage,
+                                 const ModT* msc) {
   const int n = c.tid / SROW, part = c.tid % SROW;
-  const ModT* msh = msc + H;
   char* xrow = cX(p, c) + (size_t)n * XS * 2;
   const bool live = n < p.T;
+  u64 w0[SPAIRS], w1[SPAIRS];
+  int r = 0;
+  if (rows != nullptr) {
+    const u64* base = rows + (size_t)n * HWORDS + 2 * part;
+    auto addr = [base](int j) { return base + 2 * SROW * j; };
+    Waiter wt(p.status, p.timeout_ns);
+    issue_pairs<SPAIRS>(addr, w0, w1, live ? (1u << SPAIRS) - 1u : 0u, tag);
+    r = complete_pairs<SPAIRS>(addr, w0, w1, tag, wt);
+  } else {
+#pragma unroll
+    for (int j = 0; j < SPAIRS; ++j) {
+      const int ca = col_a_of(part + SROW * j);
+      w0[j] = *reinterpret_cast<const uint32_t*>(xrow + ca * 2);
+      w1[j] = *reinterpret_cast<const uint32_t*>(xrow + (ca + 8) * 2);
+    }
+  }
   float ss = 0.f;
-#pragma unroll 2
+#pragma unroll
   for (int j = 0; j < SPAIRS; ++j) {
-    const int ca = col_a_of(part + SROW * j);
-    const uint32_t u = *reinterpret_cast<const uint32_t*>(xrow + ca * 2);
-    const uint32_t v = *reinterpret_cast<const uint32_t*>(xrow + (ca + 8) * 2);
+    const uint32_t u = payload_of(w0[j]), v = payload_of(w1[j]);
     const float a = bf_lo(u), b = bf_hi(u), d = bf_lo(v), e = bf_hi(v);
     ss = fmaf(a, a, ss);
     ss = fmaf(b, b, ss);
@@ -349,21 +346,22 @@ __device__ void stage_adarms(const Params& p, Cta& c, const ModT* msc) {
 #pragma unroll
   for (int o = SROW / 2; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   const float rstd = rsqrtf(ss / (float)H + p.eps);
+  const ModT* msh = msc + H;
   float* res = cRes(p, c) + n * RESW;
-#pragma unroll 1
+#pragma unroll
   for (int j = 0; j < 2 * SPAIRS; ++j) {  // column pairs (ca, ca+1) then (ca+8, ca+9) of word pair j / 2
     const int col = col_a_of(part + SROW * (j >> 1)) + 8 * (j & 1);
-    uint32_t* px = reinterpret_cast<uint32_t*>(xrow + col * 2);
-    const uint32_t u = *px;
+    const uint32_t u = payload_of((j & 1) ? w1[j >> 1] : w0[j >> 1]);
     const float h0 = bf_lo(u), h1 = bf_hi(u);
     const float2 sc = mod2<ModT>(msc, col), sh = mod2<ModT>(msh, col);
     const float a0 = fmaf(h0 * rstd, 1.f + sc.x, sh.x);
     const float a1 = fmaf(h1 * rstd, 1.f + sc.y, sh.y);
-    *px = live ? pack_bf2(a0, a1) : 0u;
+    *reinterpret_cast<uint32_t*>(xrow + col * 2) = live ? pack_bf2(a0, a1) : 0u;
     // c0 and R_h are even: a column pair is entirely inside or outside the residual columns
     if (live && (unsigned)(col - c.c0) < (unsigned)c.R_h)
       *reinterpret_cast<float2*>(res + (col - c.c0)) = make_float2(h0, h1);
   }
+  return fail_code(p, c, r, stage);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -484,10 +482,14 @@ __device__ __forceinline__ float part_sum(const Params& p, const Cta& c, int j, 
   const int m = j * mtpm + (r >> 4);
   const int idx = (r & 15) * 16 + n;
   const float* P = cP(p, c) + m * 256 + idx;
-  float s = 0.f;
-#pragma unroll 1
-  for (int k = 0; k < ks; ++k) s += P[mt * k * 256];
-  return s;
+  float s[NW];  // independent loads, summed as a tree (the K-split order is fixed per geometry)
+#pragma unroll
+  for (int k = 0; k < NW; ++k) s[k] = k < ks ? P[mt * k * 256] : 0.f;
+#pragma unroll
+  for (int w = NW / 2; w >= 1; w >>= 1)
+#pragma unroll
+    for (int k = 0; k < w; ++k) s[k] += s[k + w];
+  return s[0];
 }
 
 // Epilogues ----------------------------------------------------------------------------------
@@ -592,17 +594,24 @@ __device__ __forceinline__ float dot8(const Lane8& a, const Lane8& b) {
   for (int i = 0; i < 8; ++i) s = fmaf(a.v[i], b.v[i], s);
   return group8_sum(s);
 }
-// Block-wide max of a value that is uniform within each 8-lane group.
-__device__ __forceinline__ float block_max(const Params& p, const Cta& c, float v) {
+// Block-wide max of a value that is uniform within each 8-lane group, with an OR of `fail` over
+// the block taken at the same barrier. The per-warp slots alternate with `buf` (the chunk parity):
+// a thread writing slot set b has passed the previous chunk's barrier, after which nobody reads
+// set b any more.
+__device__ __forceinline__ float block_max(const Params& p, const Cta& c, float v, int buf, int fail, int& any_fail) {
   v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 8));
   v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 16));
-  __syncthreads();
-  if (c.lane == 0) cRed(p, c)[c.warp] = v;
-  __syncthreads();
-  float m = cRed(p, c)[0];
+  float* red = cRed(p, c) + buf * NW;
+  if (c.lane == 0) red[c.warp] = v;
+  any_fail = __syncthreads_or(fail);
+  float m[NW];
 #pragma unroll
-  for (int w = 1; w < NW; ++w) m = fmaxf(m, cRed(p, c)[w]);
-  return m;
+  for (int w = 0; w < NW; ++w) m[w] = red[w];
+#pragma unroll
+  for (int w = NW / 2; w >= 1; w >>= 1)
+#pragma unroll
+    for (int k = 0; k < w; ++k) m[k] = fmaxf(m[k], m[k + w]);
+  return m[0];
 }
 
 // SA = true: self-attention (queries of row t over memory rows [cu_kv[0], PM) and the T action
@@ -662,9 +671,10 @@ __device__ __forceinline__ int attention_unit(const Params& p, Cta& c, const boo
   auto addr = [qrow, krow](int i) { return (i < 2 ? qrow : krow + (i >> 2) * HWORDS) + 2 * (i & 1); };
   Waiter wt(p.status, p.timeout_ns);
   issue_pairs<6>(addr, w0, w1, own ? 0x3fu : 0x3u, tag);
+  // A failed wait is OR-ed over the block at the first chunk's block_max barrier; until then the
+  // lanes compute on whatever they hold (registers only).
   const int rc = complete_pairs<6>(addr, w0, w1, tag, wt);
-  fail_code(p, c, rc, SA ? ST_SA : ST_CA);
-  if (__syncthreads_or(rc != 0)) return 1;
+  const int fail = fail_code(p, c, rc, SA ? ST_SA : ST_CA);
   MKX_TRACE(1);
 
   Lane8 q;
@@ -682,7 +692,9 @@ __device__ __forceinline__ int attention_unit(const Params& p, Cta& c, const boo
 
   float m_run = -INFINITY, den = 0.f;
   float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  for (int base = kbeg; base < nkeys || (SA && base == kbeg); base += NG * MAXK) {
+  int chunk = 0;
+  bool checked = false;  // the poll's failure flag went through a block_max barrier
+  for (int base = kbeg; base < nkeys || (SA && base == kbeg); base += NG * MAXK, ++chunk) {
     if (base != kbeg) load_chunk(base);
     float s[MAXK];
     float mloc = (SA && base == kbeg) ? s_own : -INFINITY;
@@ -701,7 +713,10 @@ __device__ __forceinline__ int attention_unit(const Params& p, Cta& c, const boo
       s[i] = j < nkeys ? dv : -INFINITY;
       mloc = fmaxf(mloc, s[i]);
     }
-    const float m_new = fmaxf(m_run, block_max(p, c, mloc));
+    int any_fail;
+    const float m_new = fmaxf(m_run, block_max(p, c, mloc, chunk & 1, fail, any_fail));
+    if (any_fail) return 1;
+    checked = true;
     const float alpha = __expf(m_run - m_new);  // 0 on the first chunk
     den *= alpha;
 #pragma unroll
@@ -729,33 +744,41 @@ __device__ __forceinline__ int attention_unit(const Params& p, Cta& c, const boo
     m_run = m_new;
     if (base + NG * MAXK >= nkeys) break;
   }
-  // Reduce the NG groups in two levels: o in lane order per lane, den per group.
+  if (!checked && __syncthreads_or(fail)) return 1;  // no key at all (uniform)
+  // Reduce the NG key groups: the 4 groups of a warp by shuffles (lanes l8, l8 + 8, l8 + 16, l8 + 24
+  // hold the same dims), then the NW warps' partials through shared memory. o is in lane order; den
+  // is uniform within a group. The previous reader of P finished before the stage's last barrier.
   MKX_TRACE(2);
-  __syncthreads();
-  float* ro = cP(p, c);                  // [NG][64]
-  float* rd = ro + NG * 64;              // [NG]
-  float* r2 = rd + NG;                   // [4][64] second level
-  float* r2d = r2 + 4 * 64;              // [4]
 #pragma unroll
-  for (int e = 0; e < 8; ++e) ro[kg * 64 + l8 * 8 + e] = o[e];
-  if (l8 == 0) rd[kg] = den;
-  __syncthreads();
-  if (c.tid < 256) {
-    const int slot = c.tid & 63, part = c.tid >> 6;
-    float acc = 0.f, dsum = 0.f;
-#pragma unroll 4
-    for (int gi = part * (NG / 4); gi < (part + 1) * (NG / 4); ++gi) {
-      acc += ro[gi * 64 + slot];
-      dsum += rd[gi];
-    }
-    r2[part * 64 + slot] = acc;
-    if (slot == 0) r2d[part] = dsum;
+  for (int e = 0; e < 8; ++e) {
+    o[e] += __shfl_xor_sync(0xffffffffu, o[e], 8);
+    o[e] += __shfl_xor_sync(0xffffffffu, o[e], 16);
+  }
+  den += __shfl_xor_sync(0xffffffffu, den, 8);
+  den += __shfl_xor_sync(0xffffffffu, den, 16);
+  float* ro = cP(p, c);          // [NW][64]
+  float* rd = ro + NW * 64;      // [NW]
+  if (c.lane < 8) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ro[c.warp * 64 + l8 * 8 + e] = o[e];
+    if (l8 == 0) rd[c.warp] = den;
   }
   __syncthreads();
   if (c.tid < 64) {
-    const float acc = (r2[c.tid] + r2[64 + c.tid]) + (r2[128 + c.tid] + r2[192 + c.tid]);
-    const float dsum = (r2d[0] + r2d[1]) + (r2d[2] + r2d[3]);
-    const float val = acc / dsum;
+    float acc[NW], dsum[NW];
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      acc[w] = ro[w * 64 + c.tid];
+      dsum[w] = rd[w];
+    }
+#pragma unroll
+    for (int w = NW / 2; w >= 1; w >>= 1)
+#pragma unroll
+      for (int k = 0; k < w; ++k) {
+        acc[k] += acc[k + w];
+        dsum[k] += dsum[k + w];
+      }
+    const float val = acc[0] / dsum[0];
     const float nxt = __shfl_down_sync(0xffffffffu, val, 1);
     if ((c.tid & 1) == 0)
       st_volatile(y_rows + (size_t)t * HWORDS + h * 32 + (c.tid >> 1), make_word(tag, pack_bf2(val, nxt)));
@@ -917,22 +940,21 @@ __device__ __forceinline__ int stage_norm_gemm(const Params& p, Cta& c, int whic
   const int par = gi & 1;
   const uint32_t tag = c.tag0 + (uint32_t)gi;
   u64* const* xb = p.xb;
-  if (!(which == 0 && l == 0)) {  // layer 0's h0 is already in X (step tail)
-    const u64* rows = which == 0 ? xb[B_HOUT] + (size_t)((gi - 1) & 1) * TP * HWORDS
-                                 : xb[which == 1 ? B_H2 : B_H3] + (size_t)par * TP * HWORDS;
-    const int fail = poll_rows_to_x(p, c, rows, which == 0 ? tag - 1u : tag, ST_QKV + 3 * which);
-    if (__syncthreads_or(fail)) return 1;
-  }
-  MKX_TRACE(0);
+  // Every thread waits on the modulation and weight mbarriers itself (completion makes the bulk
+  // copies visible to it), so one barrier after the staging covers all three waits.
   int fail = !wait_bar(p, c, BAR_MODS + (q & 1));
-  if (__syncthreads_or(fail)) return 1;
-  MKX_TRACE(1);
-  consumed(p, c, BAR_MODS + (q & 1));
-  stage_adarms<ModT>(p, c, mods_slot<ModT>(p, c, q));
+  const u64* rows = nullptr;  // layer 0's h0 is already in X (step tail)
+  if (!(which == 0 && l == 0))
+    rows = which == 0 ? xb[B_HOUT] + (size_t)((gi - 1) & 1) * TP * HWORDS
+                      : xb[which == 1 ? B_H2 : B_H3] + (size_t)par * TP * HWORDS;
+  fail |= stage_rows_adarms<ModT>(p, c, rows, which == 0 ? tag - 1u : tag, ST_QKV + 3 * which,
+                                  mods_slot<ModT>(p, c, q));
+  MKX_TRACE(0);
   const int slot = which == 0 ? S_QKV : (which == 1 ? S_QCA : S_GU);
-  fail = !wait_bar(p, c, slot);
+  fail |= !wait_bar(p, c, slot);
   if (__syncthreads_or(fail)) return 1;
   MKX_TRACE(2);
+  consumed(p, c, BAR_MODS + (q & 1));
   consumed(p, c, slot);
   const int R = which == 0 ? c.R_qkv : (which == 1 ? c.R_h : c.R_gu);
   mma_from_x(p, c, cSlot(p, c, slot), which == 2 ? 2 : 1, R);

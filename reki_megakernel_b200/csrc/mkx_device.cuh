@@ -129,18 +129,14 @@ __device__ __forceinline__ u64 ld_volatile(const u64* p) {
   return v;
 }
 
-__device__ __forceinline__ uint2 lds64(const void* p) {
-  uint2 v;
-  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(smem_u32(p)));
-  return v;
-}
-__device__ __forceinline__ uint32_t lds32(const void* p) {
-  uint32_t v;
-  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)));
-  return v;
-}
+// Plain shared-memory loads (not asm): the compiler may schedule them early and overlap them with
+// the MMAs of the previous k-block, and it still keeps them after the barriers that publish the data.
+__device__ __forceinline__ uint2 lds64(const void* p) { return *reinterpret_cast<const uint2*>(p); }
+__device__ __forceinline__ uint32_t lds32(const void* p) { return *reinterpret_cast<const uint32_t*>(p); }
 
 // ---- tensor-core MMA: D[16 x 8] += A[16 x 16] (row) * B[16 x 8] (col), bf16 in, fp32 accumulate ----
+// Volatile (never moved into divergent code); it has no memory clobber, so the plain shared-memory
+// operand loads around it can still be scheduled across it.
 __device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
   asm volatile(
