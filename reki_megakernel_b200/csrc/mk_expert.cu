@@ -51,7 +51,9 @@ constexpr int HWORDS = H / 2;            // exchange words per H-wide row
 constexpr int QKVWORDS = 3 * H / 2;
 constexpr int XWORDS = 32;               // exchange words per action-state row (fp32 payloads)
 constexpr int NG = NT / 8;               // attention: 8-lane key groups per CTA
-constexpr int MAXK = 8;                  // keys per group per attention chunk (NG * MAXK keys)
+constexpr int MAXK = 5;                  // keys per group per attention chunk (NG * MAXK = 160 keys); more
+                                         // key registers would spill in the attention unit
+constexpr int MAX_MEM_ROWS = 256;        // memory rows per layer (any number of chunks)
 constexpr int RESW = 8;                  // residual columns kept per CTA (o / ca-o / down rows)
 constexpr int SROW = NT / TP;            // staging threads per action row
 constexpr int SPAIRS = HWORDS / 2 / SROW; // 16-byte word pairs per staging thread
@@ -717,6 +719,7 @@ __device__ __forceinline__ int attention_unit(const Params& p, Cta& c, const boo
     const float m_new = fmaxf(m_run, block_max(p, c, mloc, chunk & 1, fail, any_fail));
     if (any_fail) return 1;
     checked = true;
+    MKX_TRACE(3);
     const float alpha = __expf(m_run - m_new);  // 0 on the first chunk
     den *= alpha;
 #pragma unroll
@@ -763,7 +766,9 @@ __device__ __forceinline__ int attention_unit(const Params& p, Cta& c, const boo
     for (int e = 0; e < 8; ++e) ro[c.warp * 64 + l8 * 8 + e] = o[e];
     if (l8 == 0) rd[c.warp] = den;
   }
+  MKX_TRACE(4);
   __syncthreads();
+  MKX_TRACE(5);
   if (c.tid < 64) {
     float acc[NW], dsum[NW];
 #pragma unroll
@@ -961,6 +966,7 @@ __device__ __forceinline__ int stage_norm_gemm(const Params& p, Cta& c, int whic
   __syncthreads();
   MKX_TRACE(3);
   if (c.tid == ISSUER && gi + 1 < p.n_steps * p.L) issue_slot(p, c, slot, (gi + 1) % p.L);
+  MKX_TRACE(4);
   if (which == 2) {
     epi_gu(p, c, xb[B_G] + (size_t)par * TP * (p.I >> 1), tag);
   } else if (which == 1) {
@@ -968,6 +974,7 @@ __device__ __forceinline__ int stage_norm_gemm(const Params& p, Cta& c, int whic
   } else if (!(p.drop_stage == ST_QKV && c.cta == 0 && gi == 0)) {
     epi_plain(p, c, c.R_qkv, c.r0_qkv, xb[B_QKV] + (size_t)par * TP * QKVWORDS, QKVWORDS, tag);
   }
+  MKX_TRACE(5);
   return 0;
 }
 
@@ -995,7 +1002,9 @@ __device__ __forceinline__ int stage_words_gemm(const Params& p, Cta& c, int whi
   u64* out = xb[which == 0 ? B_H2 : (which == 1 ? B_H3 : B_HOUT)] + (size_t)par * TP * HWORDS;
   epi_gated<ModT>(p, c, mods_slot<ModT>(p, c, q) + 2 * H, out, tag,
                   (which == 2 && p.trace_h) ? p.trace_h + (size_t)gi * p.T * H : nullptr);
+  MKX_TRACE(5);
   __syncthreads();
+  MKX_TRACE(6);
   if (c.tid == ISSUER) issue_mods<ModT>(p, c, q + 2);  // this block's last use
   return 0;
 }
@@ -1411,7 +1420,7 @@ extern "C" mkx_status mkx_run(mkx_handle* h, const mkx_step_inputs* in, cudaStre
   if (!in->x_in || !in->x_out || !in->mods || !in->dt || !in->cu_kv || !in->cu_src || !in->sa_cos || !in->sa_sin ||
       !in->ca_cos || !in->ca_sin)
     return MKX_ERR_INVALID_ARG;
-  if (in->mem_rows < 1 || in->mem_rows > NG * MAXK || in->ca_rows < 1) return MKX_ERR_UNSUPPORTED;
+  if (in->mem_rows < 1 || in->mem_rows > MAX_MEM_ROWS || in->ca_rows < 1) return MKX_ERR_UNSUPPORTED;
   if (in->mem_row_stride < H || in->mem_row_stride % 8 || in->ca_row_stride < H || in->ca_row_stride % 8)
     return MKX_ERR_INVALID_ARG;
   if (!aligned16(in->sa_cos) || !aligned16(in->sa_sin) || !aligned16(in->ca_cos) || !aligned16(in->ca_sin) ||
@@ -1588,7 +1597,7 @@ extern "C" mkx_status mkx_run_static(const mkx_dims* dims, const mkx_packed_weig
   if (!in->x_in || !in->x_out || !in->mods || !in->dt || !in->cu_kv || !in->cu_src || !in->sa_cos || !in->sa_sin ||
       !in->ca_cos || !in->ca_sin)
     return MKX_ERR_INVALID_ARG;
-  if (in->mem_rows < 1 || in->mem_rows > NG * MAXK || in->ca_rows < 1) return MKX_ERR_UNSUPPORTED;
+  if (in->mem_rows < 1 || in->mem_rows > MAX_MEM_ROWS || in->ca_rows < 1) return MKX_ERR_UNSUPPORTED;
   if (in->mem_row_stride < H || in->mem_row_stride % 8 || in->ca_row_stride < H || in->ca_row_stride % 8)
     return MKX_ERR_INVALID_ARG;
   if (!aligned16(in->sa_cos) || !aligned16(in->sa_sin) || !aligned16(in->ca_cos) || !aligned16(in->ca_sin) ||

@@ -130,6 +130,19 @@ def test_edge_shapes(small, T, adim, n_steps, S, frames):
     assert mxp <= TOL_MAX
 
 
+@pytest.mark.parametrize("frame_slots,frames_valid", [(8, 6), (8, 8)])
+def test_long_memory_several_chunks(small, frame_slots, frames_valid):
+    """256 memory rows (192 or 256 valid keys): self-attention runs over more than one key chunk."""
+    dims, w, mk, orc = small
+    inp = make_inputs(dims, T=10, n_steps=2, frame_slots=frame_slots, frames_valid=frames_valid, S=200,
+                      poison=True, seed=7)
+    out = run_mk(mk, inp)
+    ref = orc.run(inp)[0]
+    mx, mean = chunk_err(out, ref, inp.action_dim)
+    assert torch.isfinite(out).all()
+    assert mx <= TOL_MAX and mean <= TOL_MEAN, (frame_slots, frames_valid, mx, mean)
+
+
 def test_fp32_mods_bitwise_equal(small):
     """fp32 modulations holding exactly the bf16 values give bit-identical outputs."""
     dims, w, mk, _ = small
