@@ -54,6 +54,8 @@ constexpr int NG = NT / 8;               // attention: 8-lane key groups per CTA
 constexpr int MAXK = 5;                  // keys per group per attention chunk (NG * MAXK = 160 keys); more
                                          // key registers would spill in the attention unit
 constexpr int MAX_MEM_ROWS = 256;        // memory rows per layer (any number of chunks)
+constexpr int PSTR = 20;                 // partials: floats per token row of a 16-row m-tile block
+constexpr int PM = TP * PSTR;            // partials: floats per (m-tile, K-split) block
 constexpr int RESW = 8;                  // residual columns kept per CTA (o / ca-o / down rows)
 constexpr int SROW = NT / TP;            // staging threads per action row
 constexpr int SPAIRS = HWORDS / 2 / SROW; // 16-byte word pairs per staging thread
@@ -367,31 +369,50 @@ __device__ int stage_rows_adarms(const Params& p, Cta& c, const u64* rows, uint3
 }
 
 // ---------------------------------------------------------------------------------------------
+// Split of a shared-memory GEMM over the NW warps: `nmat` matrices (<= 2) of R rows (<= 32), i.e. mt
+// m-tiles of 16 rows in total (1, 2 or 4: a power of two), each K-split ks = NW / mt ways. Shifts and
+// masks only: these sit on the critical path of every stage.
+struct Split {
+  int lmtpm, lmt, lks;  // log2 of m-tiles per matrix, of m-tiles, of K-splits
+};
+__device__ __forceinline__ Split gemm_split(int nmat, int R) {
+  Split q;
+  q.lmtpm = R > 16 ? 1 : 0;
+  q.lmt = q.lmtpm + (nmat > 1 ? 1 : 0);
+  q.lks = 3 - q.lmt;  // NW = 8
+  return q;
+}
+static_assert(NW == 8, "gemm_split assumes 8 warps");
+
+// ---------------------------------------------------------------------------------------------
+// K-split partials, token-major: P[block][token n][PSTR] holds the 16 output rows of a (m-tile, K-split)
+// block for token n. The epilogue reads a lane's two rows (2pp, 2pp + 1) as one aligned float2 and
+// consecutive lanes read consecutive float2s; the MMA lanes' stores fall in distinct banks (8 cc + g).
 __device__ __forceinline__ void store_partials(const Params& p, const Cta& c, const float (&d0)[4], const float (&d1)[4]) {
   const int g = c.lane >> 2, cc = c.lane & 3;
-  float* P = cP(p, c) + c.warp * 256;
-  P[g * 16 + 2 * cc] = d0[0];
-  P[g * 16 + 2 * cc + 1] = d0[1];
-  P[(g + 8) * 16 + 2 * cc] = d0[2];
-  P[(g + 8) * 16 + 2 * cc + 1] = d0[3];
-  P[g * 16 + 8 + 2 * cc] = d1[0];
-  P[g * 16 + 8 + 2 * cc + 1] = d1[1];
-  P[(g + 8) * 16 + 8 + 2 * cc] = d1[2];
-  P[(g + 8) * 16 + 8 + 2 * cc + 1] = d1[3];
+  float* P = cP(p, c) + c.warp * PM;
+  P[(2 * cc) * PSTR + g] = d0[0];
+  P[(2 * cc + 1) * PSTR + g] = d0[1];
+  P[(2 * cc) * PSTR + g + 8] = d0[2];
+  P[(2 * cc + 1) * PSTR + g + 8] = d0[3];
+  P[(8 + 2 * cc) * PSTR + g] = d1[0];
+  P[(8 + 2 * cc + 1) * PSTR + g] = d1[1];
+  P[(8 + 2 * cc) * PSTR + g + 8] = d1[2];
+  P[(8 + 2 * cc + 1) * PSTR + g + 8] = d1[3];
 }
 
 // GEMM with the B operand (activations) from shared X: `nmat` matrices of R rows each (K = H).
 __device__ void mma_from_x(const Params& p, Cta& c, const char* wslot, int nmat, int R) {
-  const int mtpm = (R + 15) >> 4, mt = nmat * mtpm, ks = NW / mt;
+  const Split q = gemm_split(nmat, R);
   const int g = c.lane >> 2, cc = c.lane & 3;
   const bool two = p.T > 8;
   float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
-  if (c.warp < mt * ks) {
-    const int m = c.warp % mt, ksl = c.warp / mt;
-    const int j = m / mtpm, mm = m % mtpm;
+  {  // mt * ks == NW: every warp has a (m-tile, K-range)
+    const int m = c.warp & ((1 << q.lmt) - 1), ksl = c.warp >> q.lmt;
+    const int j = m >> q.lmtpm, mm = m & ((1 << q.lmtpm) - 1);
     const char* A = wslot + (size_t)j * R * H * 2 + cc * 8;
     constexpr int KB = H / 16;
-    const int kb0 = ksl * KB / ks, kb1 = (ksl + 1) * KB / ks;
+    const int kb0 = (ksl * KB) >> q.lks, kb1 = ((ksl + 1) * KB) >> q.lks;
     const int ra = mm * 16 + g, rb = ra + 8;
     const bool va = ra < R, vb = rb < R;
     const char* x0 = cX(p, c) + (size_t)g * XS * 2 + cc * 4;
@@ -478,31 +499,36 @@ __device__ int mma_from_words(const Params& p, Cta& c, const char* wslot, int R,
   return fail_code(p, c, rc, stage);
 }
 
-// Sum of the K-split partials for output row r (of matrix j), token n.
-__device__ __forceinline__ float part_sum(const Params& p, const Cta& c, int j, int R, int nmat, int r, int n) {
-  const int mtpm = (R + 15) >> 4, mt = nmat * mtpm, ks = NW / mt;
-  const int m = j * mtpm + (r >> 4);
-  const int idx = (r & 15) * 16 + n;
-  const float* P = cP(p, c) + m * 256 + idx;
-  float s[NW];  // independent loads, summed as a tree (the K-split order is fixed per geometry)
+// Sum of the K-split partials for output rows 2pp, 2pp + 1 (of matrix j), token n.
+__device__ __forceinline__ float2 part_sum2(const Params& p, const Cta& c, const Split& q, int j, int pp, int n) {
+  const int r = 2 * pp;
+  const int m = (j << q.lmtpm) + (r >> 4);
+  const float* P = cP(p, c) + m * PM + n * PSTR + (r & 15);
+  const int ks = NW >> q.lmt, mt = 1 << q.lmt;
+  float2 s[NW];  // independent loads, summed as a tree (the K-split order is fixed per geometry)
 #pragma unroll
-  for (int k = 0; k < NW; ++k) s[k] = k < ks ? P[mt * k * 256] : 0.f;
+  for (int k = 0; k < NW; ++k) s[k] = k < ks ? *reinterpret_cast<const float2*>(P + mt * k * PM) : make_float2(0.f, 0.f);
 #pragma unroll
   for (int w = NW / 2; w >= 1; w >>= 1)
 #pragma unroll
-    for (int k = 0; k < w; ++k) s[k] += s[k + w];
+    for (int k = 0; k < w; ++k) {
+      s[k].x += s[k + w].x;
+      s[k].y += s[k + w].y;
+    }
   return s[0];
 }
 
 // Epilogues ----------------------------------------------------------------------------------
 // Linear output rounded to bf16 (QKV, CA query): words of columns [col0, col0 + R).
+// Epilogue threads: e -> (column pair pp = e % npairs, action row n = e / npairs): consecutive lanes
+// publish consecutive words of a row (coalesced exchange stores).
 __device__ void epi_plain(const Params& p, const Cta& c, int R, int col0, u64* out_rows, int row_words,
                           uint32_t tag) {
-  const int npairs = R >> 1;
-  const int e = c.tid;
-  if (e < npairs * p.T) {
-    const int pp = e % npairs, n = e / npairs;
-    const float v0 = part_sum(p, c, 0, R, 1, 2 * pp, n), v1 = part_sum(p, c, 0, R, 1, 2 * pp + 1, n);
+  const int npairs = R >> 1, pp = c.tid % npairs, n = c.tid / npairs;
+  if (c.tid < npairs * p.T) {
+    const Split q = gemm_split(1, R);
+    const float2 v = part_sum2(p, c, q, 0, pp, n);
+    const float v0 = v.x, v1 = v.y;
     st_volatile(out_rows + (size_t)n * row_words + word_pos((col0 >> 1) + pp), make_word(tag, pack_bf2(v0, v1)));
   }
 }
@@ -511,13 +537,12 @@ __device__ void epi_plain(const Params& p, const Cta& c, int R, int col0, u64* o
 template <typename ModT>
 __device__ void epi_gated(const Params& p, const Cta& c, const ModT* gate, u64* out_rows, uint32_t tag,
                           uint16_t* trace) {
-  const int npairs = c.R_h >> 1;
-  const int e = c.tid;
-  if (e < npairs * p.T) {
-    const int pp = e % npairs, n = e / npairs;
+  const int npairs = c.R_h >> 1, pp = c.tid % npairs, n = c.tid / npairs;
+  if (c.tid < npairs * p.T) {
+    const Split q = gemm_split(1, c.R_h);
     const float2 gv = mod2<ModT>(gate, c.c0 + 2 * pp);
-    const float a0 = round_bf(part_sum(p, c, 0, c.R_h, 1, 2 * pp, n));
-    const float a1 = round_bf(part_sum(p, c, 0, c.R_h, 1, 2 * pp + 1, n));
+    const float2 v = part_sum2(p, c, q, 0, pp, n);
+    const float a0 = round_bf(v.x), a1 = round_bf(v.y);
     const float o0 = fmaf(a0, gv.x, cRes(p, c)[n * RESW + 2 * pp]);
     const float o1 = fmaf(a1, gv.y, cRes(p, c)[n * RESW + 2 * pp + 1]);
     const uint32_t pl = pack_bf2(o0, o1);
@@ -528,16 +553,16 @@ __device__ void epi_gated(const Params& p, const Cta& c, const ModT* gate, u64* 
 
 // g = bf16(silu(bf16(gate)) * bf16(up)) (src/mk_expert.py:403-413).
 __device__ void epi_gu(const Params& p, const Cta& c, u64* out_rows, uint32_t tag) {
-  const int R = c.R_gu, npairs = R >> 1, row_words = p.I >> 1;
-  const int e = c.tid;
-  if (e < npairs * p.T) {
-    const int pp = e % npairs, n = e / npairs;
+  const int R = c.R_gu, row_words = p.I >> 1;
+  const int npairs = R >> 1, pp = c.tid % npairs, n = c.tid / npairs;
+  if (c.tid < npairs * p.T) {
+    const Split q = gemm_split(2, R);
+    const float2 gv = part_sum2(p, c, q, 0, pp, n), uv = part_sum2(p, c, q, 1, pp, n);
     float o[2];
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
-      const int r = 2 * pp + k;
-      const float gf = round_bf(part_sum(p, c, 0, R, 2, r, n));
-      const float uf = round_bf(part_sum(p, c, 1, R, 2, r, n));
+      const float gf = round_bf(k ? gv.y : gv.x);
+      const float uf = round_bf(k ? uv.y : uv.x);
       o[k] = __fdividef(gf, 1.f + __expf(-gf)) * uf;
     }
     st_volatile(out_rows + (size_t)n * row_words + word_pos((c.u0 >> 1) + pp), make_word(tag, pack_bf2(o[0], o[1])));
@@ -1280,8 +1305,8 @@ static Layout make_layout(int I, int G) {
   ly.s_slot[S_GU] = take(ly.max_rows_gu * H * 4);
   ly.s_slot[S_D] = take(ly.max_rows_h * I * 2);
   ly.s_x = take(TP * XS * 2);
-  constexpr int attn_floats = NG * 64 + NG + 4 * 64 + 4;  // attention reductions, two levels
-  ly.s_p = take((attn_floats > NW * 256 ? attn_floats : NW * 256) * 4);
+  constexpr int attn_floats = NW * 64 + NW;  // attention output reduction: per-warp o and den
+  ly.s_p = take((attn_floats > NW * PM ? attn_floats : NW * PM) * 4);
   ly.s_mods = take(2 * 3 * H * 4);  // sized for fp32 modulations
   ly.s_xs = take(TP * 32 * 4);
   ly.s_res = take(TP * RESW * 4);
@@ -1316,7 +1341,8 @@ extern "C" mkx_status mkx_create(const mkx_dims* dims, const mkx_weights* w, int
   if (G < d.A || G < TP || G > H / 2 || G > sms) return MKX_ERR_RESOURCES;
   if (min_part(d.I / 2, G) < 1) return MKX_ERR_RESOURCES;
   const Layout ly = make_layout(d.I, G);
-  // one epilogue element (column pair, action row) per thread
+  // one epilogue element (column pair, action row) per thread; this also keeps every matrix at <= 32
+  // rows per CTA, the bound gemm_split assumes
   if (ly.max_rows_qkv / 2 * TP > NT || ly.max_rows_h > RESW || ly.max_rows_gu / 2 * TP > NT) return MKX_ERR_RESOURCES;
   if (ly.total > smem_optin) return MKX_ERR_RESOURCES;
 
