@@ -181,6 +181,51 @@ def run_reference(args, rank: int, world: int):
 
 
 # ------------------------------------------------------------------------------------------------
+STAGE_NAMES = ["qkv", "sa", "o", "ca_q", "ca", "ca_o", "gate_up", "down"]
+
+
+def run_timeline(args):
+    """Per-stage critical path of one predict from the kernel's stage stamps
+    (thread 0 of every CTA stamps %globaltimer at the end of each stage, as the reference's PROFILE
+    mode does): for each stage, end of the last CTA minus end of the last CTA in the previous stage,
+    median over layers and Euler steps. Not a bench line: the stamps add a store per stage."""
+    from reki_megakernel_b200.mk_expert import ExpertMegakernel
+    from reki_megakernel_b200.synthetic import ExpertDims, make_inputs, make_past, make_weights
+    dims = ExpertDims()
+    mk = ExpertMegakernel(weights=make_weights(dims, seed=0).to("cuda"))
+    inp = make_inputs(dims).to("cuda")
+    past = make_past(inp)
+    n = inp.n_steps
+    stride = 1 + mk.barriers(n)
+    prof = torch.zeros(mk.nprog * stride, dtype=torch.int64, device="cuda")
+    runs = []
+    for _ in range(args.warmup + args.steps):
+        prof.zero_()
+        mk.run(inp.x[:1], inp.mods[0], inp.dt[:1], past, inp.action_dim, prof=prof)
+        torch.cuda.synchronize()
+        mk.check_device_error()
+        runs.append(prof.view(mk.nprog, stride).cpu())
+    per = {}
+    for a in runs[args.warmup:]:
+        ends = a[:, 1:]
+        last = ends.max(dim=0).values
+        prev = a[:, 0].min()
+        for k in range(ends.shape[1]):
+            if k == 0:
+                name = "first_tail"
+            else:
+                j = (k - 1) % (8 * dims.L + 1)
+                name = "step_tail" if j == 8 * dims.L else STAGE_NAMES[j % 8]
+            per.setdefault(name, []).append(float(last[k] - prev) / 1e3)
+            prev = last[k]
+    total = [float(a[:, 1:].max() - a[:, 0].min()) / 1e3 for a in runs[args.warmup:]]
+    out = {"timeline_us": {k: round(statistics.median(v), 3) for k, v in per.items()},
+           "per_layer_us": round(sum(statistics.median(per[k]) for k in STAGE_NAMES), 3),
+           "predict_us": round(statistics.median(total), 1), "predicts": len(total),
+           "config": "REKI expert steps 2-10, T=10, S=160, 64 memory rows, batch 1"}
+    print(json.dumps(out), flush=True)
+
+
 def run_mk(args, rank: int, world: int):
     from reki_megakernel_b200.mk_expert import ExpertMegakernel
     from reki_megakernel_b200.synthetic import ExpertDims, make_inputs, make_past, make_weights
@@ -331,11 +376,16 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--max-ref-steps", type=int, default=60)
+    ap.add_argument("--timeline", action="store_true", help="per-stage critical path of one predict, no bench line")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.timeline:
+        if rank == 0:
+            run_timeline(args)
+        return
     if world > 1:
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         backend = "nccl" if args.impl == "mk" else "gloo"
