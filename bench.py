@@ -153,7 +153,7 @@ def run_reference(args, rank: int, world: int):
     from reki_megakernel_b200.synthetic import make_inputs, make_weights
     torch.set_num_threads(threads)
     orc = OracleExpert(make_weights(dims, seed=0), "fp32")
-    inp = make_inputs(dims, n_steps=1)
+    inp = make_inputs(dims, n_steps=1, S=args.S)
     e = inp.episode(0)
     ep = dict(x=e.x[0], mods=e.mods[0], dt=e.dt[0], memk=e.memk[0], memv=e.memv[0], kv_start=int(e.kv_start[0]),
               kca=e.kca[0], vca=e.vca[0], S=int(e.S[0]), sa_cos=e.sa_cos[0], sa_sin=e.sa_sin[0],
@@ -172,7 +172,7 @@ def run_reference(args, rank: int, world: int):
         "steps": steps, "warmup": args.warmup, "ms_per_step": ms_predict, "ms_per_predict": ms_predict,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": "REKI expert steps 2-10, batch 1 (BASELINE configs[1] shapes), CPU fp32 eager",
-                   "T": 10, "S": 160, "memory_rows": 64, "euler_steps": 9},
+                   "T": 10, "S": args.S, "memory_rows": 64, "euler_steps": 9},
         "cpu_baseline": {"value": value, "unit": "episodes/s", "cores": threads, "kind": "port",
                          "sample": f"{steps} Euler steps of one episode (x9 = ms per predict), fp32 oracle"},
         "e2e": {"value": value, "unit": "episodes/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -226,7 +226,27 @@ def run_timeline(args):
     print(json.dumps(out), flush=True)
 
 
+def episodes_of_rank(rank: int, batch: int) -> list[int]:
+    """Global episode indices served by this rank: ranks own disjoint, consecutive blocks of
+    `batch` episodes, each seeded by its index."""
+    return list(range(rank * batch, (rank + 1) * batch))
+
+
+def max_over_ranks(vals, world: int, device) -> list[float]:
+    """Element-wise max over ranks (the slowest rank bounds the job's time)."""
+    t = torch.tensor([float(v) for v in vals], dtype=torch.float64, device=device)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return [float(x) for x in t]
+
+
+def job_episodes_per_s(world: int, batch: int, ms_per_step: float) -> float:
+    """Whole-job throughput: every rank finishes `batch` episodes per step of `ms_per_step`."""
+    return world * batch * 1000.0 / ms_per_step
+
+
 def run_mk(args, rank: int, world: int):
+    from types import SimpleNamespace
     from reki_megakernel_b200.mk_expert import ExpertMegakernel
     from reki_megakernel_b200.synthetic import ExpertDims, make_inputs, make_past, make_weights
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -236,16 +256,15 @@ def run_mk(args, rank: int, world: int):
     w = make_weights(dims, seed=0)
     mk = ExpertMegakernel(weights=w.to(dev))
     del w
-    # this rank's episodes: seeds by global episode index
-    ep0 = rank * args.batch
-    inp = make_inputs(dims, seed=ep0, noise_seed=1234 + ep0).to(dev)
-    past = make_past(inp)
-    x1, mods, dt = inp.x[:1], inp.mods[0], inp.dt[:1]
+    # this rank's episodes, one batch-1 predict each per step (the kernel serves one episode per launch)
+    eps = episodes_of_rank(rank, args.batch)
+    inps = [make_inputs(dims, S=args.S, seed=e, noise_seed=1234 + e).to(dev) for e in eps]
+    pasts = [make_past(i) for i in inps]
 
     def call():
-        return mk.run(x1, mods, dt, past, inp.action_dim)
+        return [mk.run(i.x[:1], i.mods[0], i.dt[:1], pa, i.action_dim) for i, pa in zip(inps, pasts)]
 
-    # CUDA graph of one predict's steps 2..10, as the expert graph holds it in production
+    # CUDA graph of one step (steps 2..10 of every episode of this rank), as the expert graph holds it
     s = torch.cuda.Stream(dev)
     s.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.stream(s):
@@ -254,7 +273,7 @@ def run_mk(args, rank: int, world: int):
     torch.cuda.current_stream(dev).wait_stream(s)
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
-        out = call()
+        outs = call()
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
@@ -285,29 +304,33 @@ def run_mk(args, rank: int, world: int):
     mk.check_device_error()
     per = [a.elapsed_time(b) for a, b in evs]
     ms = statistics.mean(per)
-    # end to end through the public API: H2D of every per-call input from pinned host memory,
-    # the launch, D2H of the result; timed with events on the stream
-    from types import SimpleNamespace
-    rs = past.register_step
-    dev_in = {"x": x1, "mods": mods, "dt": dt, "memk": inp.memk[0], "memv": inp.memv[0], "kca": inp.kca[0],
-              "vca": inp.vca[0], "cu_kv": rs["cu_kv"], "cu_src": rs["cu_src"], "sa_cos": inp.sa_cos[0],
-              "sa_sin": inp.sa_sin[0], "ca_cos": inp.ca_cos[0], "ca_sin": inp.ca_sin[0]}
-    host = {k: v.cpu().contiguous().pin_memory() for k, v in dev_in.items()}
-    h2d = sum(v.numel() * v.element_size() for v in host.values())
-    out_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    d2h = out_host.numel() * out_host.element_size()
-    bufs = {k: torch.empty_like(v, device=dev) for k, v in host.items()}
-    past_b = SimpleNamespace(
-        register_step={"mem_kv": [(bufs["memk"][l], bufs["memv"][l]) for l in range(dims.L)],
-                       "sa_pe": (bufs["sa_cos"], bufs["sa_sin"]), "ca_pe": (bufs["ca_cos"], bufs["ca_sin"]),
-                       "cu_kv": bufs["cu_kv"], "cu_src": bufs["cu_src"]},
-        cross_attn_kv=[(bufs["kca"][l], bufs["vca"][l]) for l in range(dims.L)])
+    # end to end through the public API: every step copies each episode's per-call inputs from
+    # pinned host memory, launches, and reads each result back; timed with events on the stream
+    hosts, bufs, pbs = [], [], []
+    for i, pa in zip(inps, pasts):
+        rs = pa.register_step
+        dev_in = {"x": i.x[:1], "mods": i.mods[0], "dt": i.dt[:1], "memk": i.memk[0], "memv": i.memv[0],
+                  "kca": i.kca[0], "vca": i.vca[0], "cu_kv": rs["cu_kv"], "cu_src": rs["cu_src"],
+                  "sa_cos": i.sa_cos[0], "sa_sin": i.sa_sin[0], "ca_cos": i.ca_cos[0], "ca_sin": i.ca_sin[0]}
+        h = {k: v.cpu().contiguous().pin_memory() for k, v in dev_in.items()}
+        bb = {k: torch.empty_like(v, device=dev) for k, v in h.items()}
+        hosts.append(h)
+        bufs.append(bb)
+        pbs.append(SimpleNamespace(
+            register_step={"mem_kv": [(bb["memk"][l], bb["memv"][l]) for l in range(dims.L)],
+                           "sa_pe": (bb["sa_cos"], bb["sa_sin"]), "ca_pe": (bb["ca_cos"], bb["ca_sin"]),
+                           "cu_kv": bb["cu_kv"], "cu_src": bb["cu_src"]},
+            cross_attn_kv=[(bb["kca"][l], bb["vca"][l]) for l in range(dims.L)]))
+    h2d = sum(v.numel() * v.element_size() for h in hosts for v in h.values())
+    out_hosts = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs]
+    d2h = sum(o.numel() * o.element_size() for o in out_hosts)
 
     def e2e_call():
-        for k in host:
-            bufs[k].copy_(host[k], non_blocking=True)
-        o = mk.run(bufs["x"], bufs["mods"], bufs["dt"], past_b, inp.action_dim)
-        out_host.copy_(o, non_blocking=True)
+        for h, bb, pb, i, oh in zip(hosts, bufs, pbs, inps, out_hosts):
+            for k in h:
+                bb[k].copy_(h[k], non_blocking=True)
+            o = mk.run(bb["x"], bb["mods"], bb["dt"], pb, i.action_dim)
+            oh.copy_(o, non_blocking=True)
 
     for _ in range(max(3, args.warmup // 4)):
         e2e_call()
@@ -325,36 +348,35 @@ def run_mk(args, rank: int, world: int):
     mk.check_device_error()
     e2e_mean = statistics.mean(e2e_ms)
 
-    # max over ranks
-    t = torch.tensor([ms, e2e_mean], dtype=torch.float64, device=dev)
-    if world > 1:
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    ms_max, e2e_max = float(t[0]), float(t[1])
+    ms_max, e2e_max = max_over_ranks([ms, e2e_mean], world, dev)
     if rank != 0:
         return
     hbm, peak_kind = peaks()
     mods_row = dims.MODW * 2
     bytes_step = algorithmic_bytes_per_step(dims, mods_row)
-    achieved = 9 * bytes_step / (ms * 1e-3) / 1e9
-    value = world * args.batch * 1000.0 / ms_max
+    # one launch streams the weights once: per-launch bytes over per-launch time
+    achieved = 9 * bytes_step / (ms / args.batch * 1e-3) / 1e9
     line = {
-        "metric": METRIC, "value": value, "unit": "episodes/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_max, "ms_per_predict": ms_max,
-        "ms_per_predict_p50": statistics.median(per), "ms_per_predict_p99": sorted(per)[min(len(per) - 1, int(0.99 * len(per)))],
+        "metric": METRIC, "value": job_episodes_per_s(world, args.batch, ms_max), "unit": "episodes/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
+        "ms_per_predict": ms_max / args.batch,
+        "ms_per_step_p50": statistics.median(per), "ms_per_step_p99": sorted(per)[min(len(per) - 1, int(0.99 * len(per)))],
         "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": (1000.0 / ms_max) / (1000.0 / PUBLISHED_MS),
+        "vs_baseline": job_episodes_per_s(world, args.batch, ms_max) / (1000.0 / PUBLISHED_MS),
         "dtype": "bf16", "data": "synthetic (seeded N(0,0.02) weights, BASELINE configs[1] shapes)",
-        "config": {"workload": "REKI expert Euler steps 2-10, batch 1 per GPU (BASELINE configs[1])",
-                   "T": 10, "S": 160, "memory_rows": 64, "euler_steps": 9, "episodes_per_gpu": args.batch,
+        "config": {"workload": "REKI expert Euler steps 2-10 (BASELINE configs[1]); one step = one predict of each "
+                               "of this GPU's episodes, batch-1 launches back to back",
+                   "T": 10, "S": args.S, "memory_rows": 64, "euler_steps": 9, "episodes_per_gpu": args.batch,
                    "parallelism": f"replicas x{world}, no collective",
-                   "l2": "256 MB written between timed predicts (untimed); weights (212 MB/step) exceed L2",
-                   "timing": "CUDA-graph replay, CUDA events per predict, mean over steps, max over ranks"},
+                   "l2": "256 MB written between timed steps (untimed); weights (212 MB/Euler step) exceed L2",
+                   "timing": "CUDA-graph replay, CUDA events per step, mean over steps, max over ranks"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                     "peak_kind": f"{peak_kind} (hbm copy, burst)", "traffic": traffic_from_profile(),
+                     "peak_kind": f"{peak_kind} (hbm copy, burst)",
+                     "traffic": traffic_from_profile() if args.S == 160 else None,
                      "algorithmic_bytes_per_launch": 9 * bytes_step},
-        "e2e": {"value": world * args.batch * 1000.0 / e2e_max, "unit": "episodes/s",
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_predict": e2e_max},
-        "gpu_launches": args.steps,
+        "e2e": {"value": job_episodes_per_s(world, args.batch, e2e_max), "unit": "episodes/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_max},
+        "gpu_launches": args.steps * args.batch,
         "clocks": clk,
         "wall_s_timed_region": wall,
     }
@@ -372,7 +394,8 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="mk", choices=["mk", "reference"])
-    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--batch", type=int, default=1, help="episodes per GPU (one batch-1 launch each per step)")
+    ap.add_argument("--S", type=int, default=160, help="cross-attention source rows (BASELINE configs[3]: 128-1024)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--max-ref-steps", type=int, default=60)
