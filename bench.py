@@ -412,9 +412,12 @@ def main():
     if world > 1:
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         backend = "nccl" if args.impl == "mk" else "gloo"
+        kw = {}
         if backend == "nccl":
-            torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
-        torch.distributed.init_process_group(backend, timeout=timedelta(seconds=120))
+            local = int(os.environ.get("LOCAL_RANK", "0"))
+            torch.cuda.set_device(local)
+            kw["device_id"] = torch.device("cuda", local)
+        torch.distributed.init_process_group(backend, timeout=timedelta(seconds=120), **kw)
     try:
         if args.impl == "reference":
             run_reference(args, rank, world)
