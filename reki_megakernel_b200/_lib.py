@@ -1,4 +1,4 @@
-"""ctypes binding of ``libmkx.so`` (declarations in ``include/mkx.h``).
+"""ctypes binding of ``libmkx.so`` (declarations in ``include/mkx.h`` and ``include/mkx_prepare.h``).
 
 The library is built in-tree by ``reki_megakernel_b200.build``. There is no fallback: if the
 library is missing or does not load, importing this module raises.
@@ -44,6 +44,11 @@ class PackedWeights(C.Structure):
     _fields_ = [("w", P * 6), ("nrm", P), ("tailw", P), ("wout", P)]
 
 
+class PrepDims(C.Structure):
+    _fields_ = [("L", C.c_int), ("H", C.c_int), ("NH", C.c_int), ("HD", C.c_int), ("src_dim", C.c_int),
+                ("eps", C.c_float)]
+
+
 SIGNATURES = {
     "mkx_create": (C.c_int, [C.POINTER(Dims), C.POINTER(Weights), C.c_int, C.POINTER(P)]),
     "mkx_run": (C.c_int, [P, C.POINTER(StepInputs), P]),
@@ -56,6 +61,10 @@ SIGNATURES = {
     "mkx_run_static": (C.c_int, [C.POINTER(Dims), C.POINTER(PackedWeights), C.POINTER(StepInputs), P, P]),
     "mkx_last_cuda_error": (C.c_char_p, []),
     "mkx_destroy": (None, [P]),
+    "mkx_prep_create": (C.c_int, [C.POINTER(PrepDims), P, P, C.c_int, C.POINTER(P)]),
+    "mkx_prep_run": (C.c_int, [P, P, C.c_int, P, P, P, P, C.c_int, P]),
+    "mkx_prep_last_error": (C.c_int, [P, C.POINTER(C.c_int)]),
+    "mkx_prep_destroy": (None, [P]),
 }
 
 _LIB = None

@@ -16,8 +16,8 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 LIB = PKG / "libmkx.so"
-SOURCES = [PKG / "csrc" / "mk_expert.cu"]
-HEADERS = [PKG / "csrc" / "mkx_device.cuh", ROOT / "include" / "mkx.h"]
+SOURCES = [PKG / "csrc" / "mk_expert.cu", PKG / "csrc" / "mk_prepare.cu"]
+HEADERS = [PKG / "csrc" / "mkx_device.cuh", ROOT / "include" / "mkx.h", ROOT / "include" / "mkx_prepare.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -40,7 +40,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         return LIB
     tmp = LIB.with_suffix(f".so.tmp{os.getpid()}")
     cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
-           "-I", str(ROOT / "include"), "-o", str(tmp), *map(str, SOURCES)]
+           "-I", str(ROOT / "include"), "-I", str(PKG / "csrc"), "-o", str(tmp), *map(str, SOURCES)]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     r = subprocess.run(cmd, capture_output=True, text=True)

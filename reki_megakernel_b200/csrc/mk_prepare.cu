@@ -1,0 +1,378 @@
+// Cross-attention K/V preparation ("register_prepare", restated; see include/mkx_prepare.h) on
+// sm_100a as one tensor-core GEMM over all layers:
+//
+//   D[f, n] = sum_k Wkv[f, k] * src[n, k]      f over [L][K|V][768] (15,360 rows at REKI's sizes)
+//
+// One CTA per (128-feature tile, block of <= 256 tokens). Warp 0: TMA producer (128-byte swizzled
+// K-major tiles of W and src, 4-stage mbarrier ring). Warp 1: allocates 256 TMEM columns and issues
+// tcgen05.mma kind::f16 (M = 128, N = tokens, K = 16 per instruction, bf16 in, fp32 accumulate in
+// TMEM), committing each stage back to the producer. Warps 2-5 (one per TMEM lane quarter): read the
+// accumulator with tcgen05.ld, transpose it through shared memory (reusing the drained stage ring),
+// then per token apply the K head RMSNorm (1 + kn) and rotate-half RoPE in fp32, round once to bf16
+// and store rows of the [L][SP][NH][HD] outputs. Every wait is bounded by %globaltimer; after a
+// timeout the CTA records the error, drains its copies and MMAs, frees TMEM and returns.
+#include <cstdint>
+#include <cstring>
+#include <new>
+#include <cuda.h>  // CUtensorMap and its enums (the encoder itself comes from cudaGetDriverEntryPoint)
+#include <cuda_runtime.h>
+
+#include "mkx_prepare.h"
+#include "mkx_device.cuh"
+
+namespace mkxp {
+using namespace mkx;
+
+constexpr int BM = 128;             // output features per tile (UMMA M)
+constexpr int BK = 64;              // K elements per stage: one 128-byte swizzle row
+constexpr int MAXN = 256;           // tokens per tile (UMMA N)
+constexpr int STAGES = 4;
+constexpr int NTHREADS = 192;       // warp 0 TMA, warp 1 TMEM + MMA, warps 2-5 epilogue
+constexpr int TMEM_COLS = 256;
+constexpr int TS = BM + 1;          // transposed tile: floats per token row (conflict-free)
+constexpr int A_BYTES = BM * BK * 2;
+constexpr int H = 768, NH = 12, HD = 64;
+constexpr int TILES_PER_LAYER = 2 * H / BM;  // 6 K tiles then 6 V tiles
+
+struct PrepParams {
+  int S, SP, ntok, L, ktiles;
+  float eps;
+  const float* kn;
+  const float* cos;
+  const float* sin;
+  uint16_t* k_out;
+  uint16_t* v_out;
+  int* status;
+  unsigned long long timeout_ns;
+};
+
+__device__ __forceinline__ bool wait_bounded(uint64_t* bar, uint32_t parity, unsigned long long limit) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity))
+    if (globaltimer() - t0 > limit) return false;
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major, 128-byte-swizzled tile (rows of 64 bf16, 8-row
+// groups 1024 bytes apart): start address >> 4, leading offset 1 (unused by this layout), stride
+// offset 1024 >> 4, descriptor version 1, layout type 2 = SWIZZLE_128B.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+  return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)64 << 32) | ((uint64_t)1 << 46) |
+         ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor of tcgen05.mma kind::f16: fp32 accumulator, bf16 A and B, both K-major,
+// N >> 3 at bit 17, M >> 4 at bit 24.
+__host__ __device__ __forceinline__ uint32_t instr_desc(int M, int N) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tmem_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+// 32 lanes x 32 consecutive columns of fp32 from TMEM (lane quarter of the calling warp).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void record(const PrepParams& p, int code) { atomicCAS(p.status, 0, code); }
+
+extern __shared__ __align__(1024) char psmem[];
+
+__global__ void __launch_bounds__(NTHREADS, 1)
+    prep_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap ts,
+                const __grid_constant__ PrepParams p) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x, tok0 = blockIdx.y * p.ntok;
+  const int stage_bytes = A_BYTES + p.ntok * BK * 2;  // a multiple of 1024
+  // every stage's A and B tile must start on a 1024-byte boundary (128-byte swizzle atoms): align the
+  // ring inside the dynamic allocation, which is sized with 1 KB to spare
+  char* ring = psmem + ((1024u - (smem_u32(psmem) & 1023u)) & 1023u);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + STAGES * stage_bytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* done = bars + 2 * STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 1);
+  int* consumed_slot = reinterpret_cast<int*>(tmem_slot + 1);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    *consumed_slot = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  __syncthreads();
+  tmem_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  int issued = 0;
+
+  if (warp == 0 && lane == 0) {
+    // producer
+    for (int kb = 0; kb < p.ktiles; ++kb) {
+      const int s = kb % STAGES;
+      if (kb >= STAGES && !wait_bounded(&empty[s], ((kb / STAGES) & 1) ^ 1, p.timeout_ns)) {
+        record(p, 0x100 | 1);
+        break;
+      }
+      char* a = ring + s * stage_bytes;
+      mbar_expect_tx(&full[s], (uint32_t)stage_bytes);
+      tma_load_2d(a, &tw, kb * BK, tile * BM, &full[s]);
+      tma_load_2d(a + A_BYTES, &ts, kb * BK, tok0, &full[s]);
+      issued = kb + 1;
+    }
+  } else if (warp == 1 && lane == 0) {
+    // MMA issuer
+    const uint32_t idesc = instr_desc(BM, p.ntok);
+    int kb = 0;
+    for (; kb < p.ktiles; ++kb) {
+      const int s = kb % STAGES;
+      if (!wait_bounded(&full[s], (kb / STAGES) & 1, p.timeout_ns)) {
+        record(p, 0x100 | 2);
+        break;
+      }
+      tmem_fence_after();
+      const uint32_t a = smem_u32(ring + s * stage_bytes), b = a + A_BYTES;
+#pragma unroll
+      for (int k = 0; k < BK / 16; ++k)
+        umma_bf16(tmem, sw128_desc(a + 32 * k), sw128_desc(b + 32 * k), idesc, (kb | k) != 0 ? 1u : 0u);
+      umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+    }
+    *consumed_slot = kb;
+    umma_commit(done);  // every MMA issued above has completed when `done` flips
+  } else if (warp >= 2) {
+    // epilogue: TMEM -> transposed fp32 tile in the (drained) stage ring -> norm / RoPE -> bf16 rows
+    const bool ok = __all_sync(0xffffffffu, wait_bounded(done, 0, p.timeout_ns));  // warp-uniform for tcgen05.ld
+    if (!ok && lane == 0) record(p, 0x100 | 3);
+    tmem_fence_after();
+    float* tsm = reinterpret_cast<float*>(ring);
+    const int q = warp & 3, r = 32 * q + lane;  // this thread's accumulator row (feature)
+    const int nvalid = min(p.ntok, p.S - tok0);
+    if (ok) {
+      for (int c0 = 0; c0 < p.ntok; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) tsm[(c0 + j) * TS + r] = __uint_as_float(v[j]);
+      }
+    }
+    tmem_fence_before();
+    asm volatile("bar.sync 1, 128;" ::: "memory");  // the 4 epilogue warps
+    if (ok) {
+      const int l = tile / TILES_PER_LAYER, within = tile % TILES_PER_LAYER;
+      const bool is_k = within < TILES_PER_LAYER / 2;
+      const int h0 = 2 * (within % (TILES_PER_LAYER / 2));
+      uint16_t* out = is_k ? p.k_out : p.v_out;
+      const float* kn = p.kn + (size_t)l * HD;
+      for (int nl = threadIdx.x - 64; nl < nvalid; nl += 128) {
+        const int n = tok0 + nl;
+#pragma unroll 1
+        for (int hh = 0; hh < 2; ++hh) {
+          const float* x = tsm + nl * TS + 64 * hh;
+          float y[HD];
+          if (is_k) {
+            float ss = 0.f;
+#pragma unroll
+            for (int d = 0; d < HD; ++d) ss = fmaf(x[d], x[d], ss);
+            const float rstd = rsqrtf(ss / (float)HD + p.eps);
+#pragma unroll
+            for (int d = 0; d < HD; ++d) y[d] = x[d] * rstd * (1.f + __ldg(kn + d));
+            const float* cs = p.cos + (size_t)n * HD;
+            const float* sn = p.sin + (size_t)n * HD;
+            float z[HD];
+#pragma unroll
+            for (int d = 0; d < HD; ++d) {
+              const float rot = d < HD / 2 ? -y[d + HD / 2] : y[d - HD / 2];
+              z[d] = fmaf(y[d], __ldg(cs + d), rot * __ldg(sn + d));
+            }
+#pragma unroll
+            for (int d = 0; d < HD; ++d) y[d] = z[d];
+          } else {
+#pragma unroll
+            for (int d = 0; d < HD; ++d) y[d] = x[d];
+          }
+          uint4* dst = reinterpret_cast<uint4*>(out + (((size_t)l * p.SP + n) * NH + h0 + hh) * HD);
+#pragma unroll
+          for (int c = 0; c < HD / 8; ++c)
+            dst[c] = make_uint4(pack_bf2(y[8 * c], y[8 * c + 1]), pack_bf2(y[8 * c + 2], y[8 * c + 3]),
+                                pack_bf2(y[8 * c + 4], y[8 * c + 5]), pack_bf2(y[8 * c + 6], y[8 * c + 7]));
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // after a failure: let every bulk copy this CTA issued land before its shared memory goes away
+    for (int kb = *consumed_slot; kb < issued; ++kb)
+      if (!wait_bounded(&full[kb % STAGES], (kb / STAGES) & 1, p.timeout_ns)) break;
+  }
+  if (warp == 1) {
+    wait_bounded(done, 0, p.timeout_ns);  // no MMA may still write the accumulator
+    tmem_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encoder() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(f);
+  }
+  return fn;
+}
+
+// bf16 matrix [rows][cols] (row-major), box of 64 columns x box_rows rows, 128-byte swizzle,
+// out-of-range rows read as zero.
+static bool encode_bf16(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  EncodeTiledFn fn = encoder();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)BK, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace mkxp
+
+struct mkx_prep_handle {
+  mkx_prep_dims d;
+  int device;
+  const uint16_t* wkv;
+  const float* kn;
+  CUtensorMap tw;
+  int* status;
+  unsigned long long timeout_ns;
+  cudaStream_t last_stream;
+};
+
+using namespace mkxp;
+
+extern "C" mkx_status mkx_prep_create(const mkx_prep_dims* dims, const uint16_t* wkv, const float* kn, int device,
+                                      mkx_prep_handle** out) {
+  if (!dims || !wkv || !kn || !out) return MKX_ERR_INVALID_ARG;
+  *out = nullptr;
+  const mkx_prep_dims d = *dims;
+  if (d.H != H || d.NH != NH || d.HD != HD || d.L < 1 || d.L > 64 || d.src_dim < BK || d.src_dim % BK != 0)
+    return MKX_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(wkv) & 15) != 0) return MKX_ERR_INVALID_ARG;
+  if (cudaSetDevice(device) != cudaSuccess) return MKX_ERR_CUDA;
+  mkx_prep_handle* h = new (std::nothrow) mkx_prep_handle();
+  if (!h) return MKX_ERR_RESOURCES;
+  memset(h, 0, sizeof(*h));
+  h->d = d;
+  h->device = device;
+  h->wkv = wkv;
+  h->kn = kn;
+  h->timeout_ns = 2000000000ull;
+  if (!encode_bf16(&h->tw, wkv, (uint64_t)d.L * 2 * H, (uint64_t)d.src_dim, BM) ||
+      cudaMalloc(&h->status, sizeof(int)) != cudaSuccess || cudaMemset(h->status, 0, sizeof(int)) != cudaSuccess ||
+      cudaFuncSetAttribute(prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           STAGES * (A_BYTES + MAXN * BK * 2) + 1024 + 64 * 8) != cudaSuccess) {
+    if (h->status) cudaFree(h->status);
+    delete h;
+    return MKX_ERR_CUDA;
+  }
+  *out = h;
+  return MKX_OK;
+}
+
+extern "C" mkx_status mkx_prep_run(mkx_prep_handle* h, const uint16_t* src, int S, const float* cos,
+                                   const float* sin, uint16_t* k_out, uint16_t* v_out, int SP, cudaStream_t stream) {
+  if (!h || !src || !cos || !sin || !k_out || !v_out) return MKX_ERR_INVALID_ARG;
+  if (S < 1 || S > 4096 || SP < S) return MKX_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(src) & 15) != 0 || (reinterpret_cast<uintptr_t>(k_out) & 15) != 0 ||
+      (reinterpret_cast<uintptr_t>(v_out) & 15) != 0)
+    return MKX_ERR_INVALID_ARG;
+  if (cudaSetDevice(h->device) != cudaSuccess) return MKX_ERR_CUDA;
+  const int ntok = S >= MAXN ? MAXN : ((S + 15) / 16) * 16;
+  CUtensorMap ts;
+  if (!encode_bf16(&ts, src, (uint64_t)S, (uint64_t)h->d.src_dim, (uint32_t)ntok)) return MKX_ERR_CUDA;
+  PrepParams p;
+  memset(&p, 0, sizeof(p));
+  p.S = S;
+  p.SP = SP;
+  p.ntok = ntok;
+  p.L = h->d.L;
+  p.ktiles = h->d.src_dim / BK;
+  p.eps = h->d.eps;
+  p.kn = h->kn;
+  p.cos = cos;
+  p.sin = sin;
+  p.k_out = k_out;
+  p.v_out = v_out;
+  p.status = h->status;
+  p.timeout_ns = h->timeout_ns;
+  // ring + alignment slack + barriers, and at least 80 KB: at most 2 CTAs per SM, so their 2 x 256
+  // TMEM columns always fit the SM's 512 and no allocation waits for another CTA
+  int smem = STAGES * (A_BYTES + ntok * BK * 2) + 1024 + 64 * 8;
+  if (smem < 80 * 1024) smem = 80 * 1024;
+  const dim3 grid(h->d.L * TILES_PER_LAYER, (S + ntok - 1) / ntok);
+  prep_kernel<<<grid, NTHREADS, smem, stream>>>(h->tw, ts, p);
+  if (cudaGetLastError() != cudaSuccess) return MKX_ERR_CUDA;
+  h->last_stream = stream;
+  return MKX_OK;
+}
+
+extern "C" mkx_status mkx_prep_last_error(mkx_prep_handle* h, int* code) {
+  if (!h || !code) return MKX_ERR_INVALID_ARG;
+  if (cudaSetDevice(h->device) != cudaSuccess || cudaStreamSynchronize(h->last_stream) != cudaSuccess ||
+      cudaMemcpy(code, h->status, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return MKX_ERR_CUDA;
+  return MKX_OK;
+}
+
+extern "C" void mkx_prep_destroy(mkx_prep_handle* h) {
+  if (!h) return;
+  cudaSetDevice(h->device);
+  if (h->status) cudaFree(h->status);
+  delete h;
+}

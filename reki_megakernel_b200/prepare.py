@@ -1,0 +1,83 @@
+"""Cross-attention K/V preparation on the GPU (``register_prepare``): every layer's K and V of the
+cross-attention stage, projected once per predict from the VLM source rows by one tcgen05 GEMM
+(``include/mkx_prepare.h``), in the layout ``ExpertMegakernel.run`` reads from
+``past.cross_attn_kv`` (src/mk_expert.py:486-495). The reference megakernel has no counterpart: it
+consumes K/V that Kyutai's model prepared (README.md:279-281).
+
+There is no CPU fallback: the CUDA library must load.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _lib
+from .synthetic import PrepareWeights, rope_cos_sin
+
+
+class RegisterPrepare:
+    """``RegisterPrepare(weights).run(src) -> (k, v)``, both [L, SP, NH, HD] bf16 on src's device."""
+
+    def __init__(self, weights: PrepareWeights, device=None):
+        self.lib = _lib.load()
+        dev = torch.device(device) if device is not None else weights.wkv.device
+        if dev.type != "cuda":
+            raise ValueError("RegisterPrepare needs CUDA tensors")
+        d = weights.dims
+        self.dims = d
+        self.device = dev
+        self.wkv = weights.wkv.to(dev, torch.bfloat16).contiguous()
+        self.kn = weights.kn.to(dev, torch.float32).contiguous()
+        pd = _lib.PrepDims(L=d.L, H=d.H, NH=d.NH, HD=d.HD, src_dim=d.src_dim, eps=float(weights.eps))
+        h = C.c_void_p()
+        _lib.check(self.lib.mkx_prep_create(C.byref(pd), self.wkv.data_ptr(), self.kn.data_ptr(),
+                                            dev.index or 0, C.byref(h)), "mkx_prep_create")
+        self.h = h
+        self._tables = {}
+
+    def tables(self, S: int):
+        """RoPE tables of source positions 0..S-1 (fp32 [S, HD])."""
+        t = self._tables.get(S)
+        if t is None:
+            c, s = rope_cos_sin(torch.arange(S), self.dims.HD)
+            t = (c.to(self.device).contiguous(), s.to(self.device).contiguous())
+            self._tables[S] = t
+        return t
+
+    def run(self, src: torch.Tensor, cos: torch.Tensor | None = None, sin: torch.Tensor | None = None,
+            SP: int | None = None, out=None):
+        d = self.dims
+        if src.dim() != 2 or src.shape[1] != d.src_dim or src.dtype != torch.bfloat16 or src.device != self.device:
+            raise ValueError(f"src must be [S, {d.src_dim}] bf16 on {self.device}")
+        src = src.contiguous()
+        S = src.shape[0]
+        SP = SP or S
+        if cos is None or sin is None:
+            cos, sin = self.tables(S)
+        if out is None:
+            k = torch.empty((d.L, SP, d.NH, d.HD), dtype=torch.bfloat16, device=self.device)
+            v = torch.empty_like(k)
+        else:
+            k, v = out
+        st = self.lib.mkx_prep_run(self.h, src.data_ptr(), S, cos.contiguous().data_ptr(), sin.contiguous().data_ptr(),
+                                   k.data_ptr(), v.data_ptr(), SP, torch.cuda.current_stream(self.device).cuda_stream)
+        _lib.check(st, "mkx_prep_run")
+        return k, v
+
+    def check_device_error(self):
+        code = C.c_int(0)
+        _lib.check(self.lib.mkx_prep_last_error(self.h, C.byref(code)), "mkx_prep_last_error")
+        if code.value != 0:
+            raise _lib.MkxError("register_prepare kernel", _lib.MKX_ERR_DEVICE, f"error word {code.value:#x}")
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.mkx_prep_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

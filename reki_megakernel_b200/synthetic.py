@@ -198,6 +198,34 @@ def register_prepare_cpu(dims: ExpertDims, src: torch.Tensor, seed: int = 0, SP:
     return k_out, v_out
 
 
+@dataclass
+class PrepareWeights:
+    """Weights of the cross-attention K/V preparation: per layer the K and V projections of the VLM
+    source, stacked as wkv [L, 2, H, src_dim] bf16 ([out, in], K first), and the K head-norm weight
+    kn [L, HD] fp32 (scale = 1 + kn)."""
+    dims: ExpertDims
+    wkv: torch.Tensor
+    kn: torch.Tensor
+    eps: float = 1e-6
+
+    def to(self, device) -> "PrepareWeights":
+        return PrepareWeights(self.dims, self.wkv.to(device), self.kn.to(device), self.eps)
+
+
+def make_prepare_weights(dims: ExpertDims = ExpertDims(), seed: int = 0) -> PrepareWeights:
+    """Seeded N(0, 0.02) projection weights (bf16) and K norm weights (bf16-representable fp32)."""
+    g = torch.Generator().manual_seed(seed + 13)
+    wkv = (torch.randn((dims.L, 2, dims.H, dims.src_dim), generator=g) * 0.02).to(torch.bfloat16)
+    kn = (torch.randn((dims.L, dims.HD), generator=g) * 0.02).to(torch.bfloat16).float()
+    return PrepareWeights(dims, wkv, kn)
+
+
+def make_source(S: int, src_dim: int = 2048, seed: int = 0) -> torch.Tensor:
+    """VLM source rows [S, src_dim] bf16: N(0, 1) x 0.5."""
+    g = torch.Generator().manual_seed(seed + 17)
+    return (torch.randn((S, src_dim), generator=g) * 0.5).to(torch.bfloat16)
+
+
 def make_inputs(dims: ExpertDims = ExpertDims(), *, B: int = 1, T: int = 10, n_steps: int = 9,
                 frame_slots: int = 3, frames_valid: int = 2, regs_per_frame: int = 32, S: int = 160,
                 SP: int | None = None, action_dim: int = 7, dt: float = 0.1, seed: int = 0,

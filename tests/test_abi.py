@@ -10,13 +10,15 @@ import pytest
 
 from conftest import ROOT
 
-HEADER = ROOT / "include" / "mkx.h"
+HEADERS = sorted((ROOT / "include").glob("*.h"))
 
 
 def declared_symbols():
-    text = HEADER.read_text()
-    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"\b(mkx_[a-z_]+)\s*\(", text)))
+    syms = set()
+    for h in HEADERS:
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        syms |= set(re.findall(r"\b(mkx_[a-z_]+)\s*\(", text))
+    return sorted(syms)
 
 
 def test_library_exports_every_declared_symbol():
@@ -39,7 +41,7 @@ def _c_layout(struct: str, fields):
     if not gcc:
         pytest.skip("gcc missing")
     body = "".join(f'printf("{f} %zu\\n", offsetof({struct}, {f}));' for f in fields)
-    src = f'#include <stdio.h>\n#include <stddef.h>\n#include "mkx.h"\nint main(void){{{body} printf("sizeof %zu\\n", sizeof({struct})); return 0;}}\n'
+    src = f'#include <stdio.h>\n#include <stddef.h>\n#include "mkx.h"\n#include "mkx_prepare.h"\nint main(void){{{body} printf("sizeof %zu\\n", sizeof({struct})); return 0;}}\n'
     import tempfile
     from pathlib import Path
     with tempfile.TemporaryDirectory() as d:
@@ -54,7 +56,7 @@ def _c_layout(struct: str, fields):
 
 
 @pytest.mark.parametrize("struct,cls", [("mkx_dims", "Dims"), ("mkx_weights", "Weights"), ("mkx_step_inputs", "StepInputs"),
-                                        ("mkx_packed_weights", "PackedWeights")])
+                                        ("mkx_packed_weights", "PackedWeights"), ("mkx_prep_dims", "PrepDims")])
 def test_struct_layout_matches_c(struct, cls):
     from reki_megakernel_b200 import _lib
     ct = getattr(_lib, cls)
@@ -81,3 +83,17 @@ def test_null_arguments_are_rejected_without_a_device():
     w = _lib.Weights(*([1] * 14))
     assert lib.mkx_create(C.byref(d), C.byref(w), 0, C.byref(h)) == _lib.MKX_ERR_UNSUPPORTED
     lib.mkx_destroy(None)
+
+
+def test_prepare_arguments_are_rejected_without_a_device():
+    from reki_megakernel_b200 import _lib
+    lib = _lib.load()
+    h = C.c_void_p()
+    assert lib.mkx_prep_create(None, None, None, 0, C.byref(h)) == _lib.MKX_ERR_INVALID_ARG
+    d = _lib.PrepDims(L=10, H=1024, NH=16, HD=64, src_dim=2048, eps=1e-6)
+    assert lib.mkx_prep_create(C.byref(d), 16, 16, 0, C.byref(h)) == _lib.MKX_ERR_UNSUPPORTED
+    d = _lib.PrepDims(L=10, H=768, NH=12, HD=64, src_dim=2000, eps=1e-6)   # not a multiple of 64
+    assert lib.mkx_prep_create(C.byref(d), 16, 16, 0, C.byref(h)) == _lib.MKX_ERR_UNSUPPORTED
+    assert lib.mkx_prep_run(None, None, 0, None, None, None, None, 0, None) == _lib.MKX_ERR_INVALID_ARG
+    assert lib.mkx_prep_last_error(None, None) == _lib.MKX_ERR_INVALID_ARG
+    lib.mkx_prep_destroy(None)
