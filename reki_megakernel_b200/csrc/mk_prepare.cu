@@ -29,7 +29,7 @@ constexpr int MAXN = 256;           // tokens per tile (UMMA N)
 constexpr int STAGES = 4;
 constexpr int NTHREADS = 192;       // warp 0 TMA, warp 1 TMEM + MMA, warps 2-5 epilogue
 constexpr int TMEM_COLS = 256;
-constexpr int TS = BM + 1;          // transposed tile: floats per token row (conflict-free)
+constexpr int TS = BM + 4;          // transposed tile: floats per token row (16-byte aligned rows)
 constexpr int A_BYTES = BM * BK * 2;
 constexpr int H = 768, NH = 12, HD = 64;
 constexpr int TILES_PER_LAYER = 2 * H / BM;  // 6 K tiles then 6 V tiles
@@ -177,14 +177,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     *consumed_slot = kb;
     umma_commit(done);  // every MMA issued above has completed when `done` flips
-  } else if (warp >= 2) {
-    // epilogue: TMEM -> transposed fp32 tile in the (drained) stage ring -> norm / RoPE -> bf16 rows
-    const bool ok = __all_sync(0xffffffffu, wait_bounded(done, 0, p.timeout_ns));  // warp-uniform for tcgen05.ld
+  }
+  // Epilogue, part 1 (warps 2-5, one per TMEM lane quarter): accumulator -> transposed fp32 tile
+  // [token][feature] in the drained stage ring.
+  float* tsm = reinterpret_cast<float*>(ring);
+  bool ok = true;
+  if (warp >= 2) {
+    ok = __all_sync(0xffffffffu, wait_bounded(done, 0, p.timeout_ns));  // warp-uniform for tcgen05.ld
     if (!ok && lane == 0) record(p, 0x100 | 3);
     tmem_fence_after();
-    float* tsm = reinterpret_cast<float*>(ring);
     const int q = warp & 3, r = 32 * q + lane;  // this thread's accumulator row (feature)
-    const int nvalid = min(p.ntok, p.S - tok0);
     if (ok) {
       for (int c0 = 0; c0 < p.ntok; c0 += 32) {
         uint32_t v[32];
@@ -194,47 +196,59 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
     }
     tmem_fence_before();
-    asm volatile("bar.sync 1, 128;" ::: "memory");  // the 4 epilogue warps
-    if (ok) {
-      const int l = tile / TILES_PER_LAYER, within = tile % TILES_PER_LAYER;
-      const bool is_k = within < TILES_PER_LAYER / 2;
-      const int h0 = 2 * (within % (TILES_PER_LAYER / 2));
-      uint16_t* out = is_k ? p.k_out : p.v_out;
-      const float* kn = p.kn + (size_t)l * HD;
-      for (int nl = threadIdx.x - 64; nl < nvalid; nl += 128) {
-        const int n = tok0 + nl;
-#pragma unroll 1
-        for (int hh = 0; hh < 2; ++hh) {
-          const float* x = tsm + nl * TS + 64 * hh;
-          float y[HD];
-          if (is_k) {
-            float ss = 0.f;
-#pragma unroll
-            for (int d = 0; d < HD; ++d) ss = fmaf(x[d], x[d], ss);
-            const float rstd = rsqrtf(ss / (float)HD + p.eps);
-#pragma unroll
-            for (int d = 0; d < HD; ++d) y[d] = x[d] * rstd * (1.f + __ldg(kn + d));
-            const float* cs = p.cos + (size_t)n * HD;
-            const float* sn = p.sin + (size_t)n * HD;
-            float z[HD];
-#pragma unroll
-            for (int d = 0; d < HD; ++d) {
-              const float rot = d < HD / 2 ? -y[d + HD / 2] : y[d - HD / 2];
-              z[d] = fmaf(y[d], __ldg(cs + d), rot * __ldg(sn + d));
-            }
-#pragma unroll
-            for (int d = 0; d < HD; ++d) y[d] = z[d];
-          } else {
-#pragma unroll
-            for (int d = 0; d < HD; ++d) y[d] = x[d];
-          }
-          uint4* dst = reinterpret_cast<uint4*>(out + (((size_t)l * p.SP + n) * NH + h0 + hh) * HD);
-#pragma unroll
-          for (int c = 0; c < HD / 8; ++c)
-            dst[c] = make_uint4(pack_bf2(y[8 * c], y[8 * c + 1]), pack_bf2(y[8 * c + 2], y[8 * c + 3]),
-                                pack_bf2(y[8 * c + 4], y[8 * c + 5]), pack_bf2(y[8 * c + 6], y[8 * c + 7]));
-        }
+  }
+  ok = __syncthreads_and(ok);  // all roles done; the tile is complete (or a wait failed)
+  // Epilogue, part 2 (all 6 warps): one (token, head) row per half-warp; lane j holds dims 4j..4j+3.
+  // K: head RMSNorm (shuffle reduction over the 16 lanes) * (1 + kn), rotate-half RoPE (partner dims
+  // d +- 32 sit in lane j ^ 8); V: as is. One bf16 rounding, 8-byte stores (128 B per row).
+  if (ok) {
+    const int l = tile / TILES_PER_LAYER, within = tile % TILES_PER_LAYER;
+    const bool is_k = within < TILES_PER_LAYER / 2;
+    const int h0 = 2 * (within % (TILES_PER_LAYER / 2));
+    uint16_t* out = is_k ? p.k_out : p.v_out;
+    const int half = lane >> 4, j = lane & 15;
+    const float4 kn = __ldg(reinterpret_cast<const float4*>(p.kn + (size_t)l * HD) + j);
+    const int nvalid = min(p.ntok, p.S - tok0);
+    const int nitems = 2 * nvalid, nw = NTHREADS / 32;
+    // item = 2 * token + head half; each warp takes two consecutive items per round
+    auto tables = [&](int it, float4& c, float4& sn) {
+      if (is_k && it < nitems) {
+        const size_t n = (size_t)(tok0 + (it >> 1));
+        c = __ldg(reinterpret_cast<const float4*>(p.cos + n * HD) + j);
+        sn = __ldg(reinterpret_cast<const float4*>(p.sin + n * HD) + j);
       }
+    };
+    float4 c = make_float4(0.f, 0.f, 0.f, 0.f), sn = c;
+    tables(2 * warp + half, c, sn);
+    for (int base = 2 * warp; base < nitems; base += 2 * nw) {  // warp-uniform: the shuffles need all lanes
+      const int it = base + half;
+      const bool valid = it < nitems;
+      float4 c2 = c, sn2 = sn;
+      tables(it + 2 * nw, c2, sn2);  // next round's tables in flight during this one
+      const int nl = it >> 1, hh = it & 1;
+      float4 y = valid ? *reinterpret_cast<const float4*>(tsm + nl * TS + 64 * hh + 4 * j)
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
+      if (is_k) {
+        float ss = fmaf(y.x, y.x, fmaf(y.y, y.y, fmaf(y.z, y.z, y.w * y.w)));
+#pragma unroll
+        for (int o = 8; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float rstd = rsqrtf(ss / (float)HD + p.eps);
+        y.x = y.x * rstd * (1.f + kn.x);
+        y.y = y.y * rstd * (1.f + kn.y);
+        y.z = y.z * rstd * (1.f + kn.z);
+        y.w = y.w * rstd * (1.f + kn.w);
+        const float sg = j < 8 ? -1.f : 1.f;  // rot[d] = -y[d + 32] for d < 32, y[d - 32] above
+        const float px = __shfl_xor_sync(0xffffffffu, y.x, 8), py = __shfl_xor_sync(0xffffffffu, y.y, 8);
+        const float pz = __shfl_xor_sync(0xffffffffu, y.z, 8), pw = __shfl_xor_sync(0xffffffffu, y.w, 8);
+        y = make_float4(fmaf(y.x, c.x, sg * px * sn.x), fmaf(y.y, c.y, sg * py * sn.y),
+                        fmaf(y.z, c.z, sg * pz * sn.z), fmaf(y.w, c.w, sg * pw * sn.w));
+      }
+      if (valid) {
+        uint2* dst = reinterpret_cast<uint2*>(out + (((size_t)l * p.SP + tok0 + nl) * NH + h0 + hh) * HD) + j;
+        *dst = make_uint2(pack_bf2(y.x, y.y), pack_bf2(y.z, y.w));
+      }
+      c = c2;
+      sn = sn2;
     }
   }
   __syncthreads();
