@@ -218,37 +218,49 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         sn = __ldg(reinterpret_cast<const float4*>(p.sin + n * HD) + j);
       }
     };
-    float4 c = make_float4(0.f, 0.f, 0.f, 0.f), sn = c;
-    tables(2 * warp + half, c, sn);
-    for (int base = 2 * warp; base < nitems; base += 2 * nw) {  // warp-uniform: the shuffles need all lanes
-      const int it = base + half;
-      const bool valid = it < nitems;
-      float4 c2 = c, sn2 = sn;
-      tables(it + 2 * nw, c2, sn2);  // next round's tables in flight during this one
-      const int nl = it >> 1, hh = it & 1;
-      float4 y = valid ? *reinterpret_cast<const float4*>(tsm + nl * TS + 64 * hh + 4 * j)
-                       : make_float4(0.f, 0.f, 0.f, 0.f);
-      if (is_k) {
-        float ss = fmaf(y.x, y.x, fmaf(y.y, y.y, fmaf(y.z, y.z, y.w * y.w)));
+    // rounds of this warp: items 2 * warp + half + 2 * nw * r; the cos/sin rows of round r + PF are
+    // loaded while round r is processed (an L2 round trip spans several rounds)
+    constexpr int PF = 4;
+    const int rounds = nitems > 2 * warp ? (nitems - 2 * warp + 2 * nw - 1) / (2 * nw) : 0;
+    const int it0 = 2 * warp + half;
+    float4 c[PF], sn[PF];
 #pragma unroll
-        for (int o = 8; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        const float rstd = rsqrtf(ss / (float)HD + p.eps);
-        y.x = y.x * rstd * (1.f + kn.x);
-        y.y = y.y * rstd * (1.f + kn.y);
-        y.z = y.z * rstd * (1.f + kn.z);
-        y.w = y.w * rstd * (1.f + kn.w);
-        const float sg = j < 8 ? -1.f : 1.f;  // rot[d] = -y[d + 32] for d < 32, y[d - 32] above
-        const float px = __shfl_xor_sync(0xffffffffu, y.x, 8), py = __shfl_xor_sync(0xffffffffu, y.y, 8);
-        const float pz = __shfl_xor_sync(0xffffffffu, y.z, 8), pw = __shfl_xor_sync(0xffffffffu, y.w, 8);
-        y = make_float4(fmaf(y.x, c.x, sg * px * sn.x), fmaf(y.y, c.y, sg * py * sn.y),
-                        fmaf(y.z, c.z, sg * pz * sn.z), fmaf(y.w, c.w, sg * pw * sn.w));
+    for (int u = 0; u < PF; ++u) {
+      c[u] = sn[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      tables(it0 + 2 * nw * u, c[u], sn[u]);
+    }
+    for (int r0 = 0; r0 < rounds; r0 += PF) {
+#pragma unroll
+      for (int u = 0; u < PF; ++u) {
+        const int r = r0 + u;
+        if (r >= rounds) break;  // warp-uniform: the shuffles need all lanes
+        const int it = it0 + 2 * nw * r;
+        const bool valid = it < nitems;
+        const int nl = it >> 1, hh = it & 1;
+        float4 y = valid ? *reinterpret_cast<const float4*>(tsm + nl * TS + 64 * hh + 4 * j)
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+        if (is_k) {
+          float ss = fmaf(y.x, y.x, fmaf(y.y, y.y, fmaf(y.z, y.z, y.w * y.w)));
+#pragma unroll
+          for (int o = 8; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+          const float rstd = rsqrtf(ss / (float)HD + p.eps);
+          y.x = y.x * rstd * (1.f + kn.x);
+          y.y = y.y * rstd * (1.f + kn.y);
+          y.z = y.z * rstd * (1.f + kn.z);
+          y.w = y.w * rstd * (1.f + kn.w);
+          const float sg = j < 8 ? -1.f : 1.f;  // rot[d] = -y[d + 32] for d < 32, y[d - 32] above
+          const float px = __shfl_xor_sync(0xffffffffu, y.x, 8), py = __shfl_xor_sync(0xffffffffu, y.y, 8);
+          const float pz = __shfl_xor_sync(0xffffffffu, y.z, 8), pw = __shfl_xor_sync(0xffffffffu, y.w, 8);
+          const float4 cc = c[u], ss4 = sn[u];
+          y = make_float4(fmaf(y.x, cc.x, sg * px * ss4.x), fmaf(y.y, cc.y, sg * py * ss4.y),
+                          fmaf(y.z, cc.z, sg * pz * ss4.z), fmaf(y.w, cc.w, sg * pw * ss4.w));
+          tables(it + 2 * nw * PF, c[u], sn[u]);
+        }
+        if (valid) {
+          uint2* dst = reinterpret_cast<uint2*>(out + (((size_t)l * p.SP + tok0 + nl) * NH + h0 + hh) * HD) + j;
+          *dst = make_uint2(pack_bf2(y.x, y.y), pack_bf2(y.z, y.w));
+        }
       }
-      if (valid) {
-        uint2* dst = reinterpret_cast<uint2*>(out + (((size_t)l * p.SP + tok0 + nl) * NH + h0 + hh) * HD) + j;
-        *dst = make_uint2(pack_bf2(y.x, y.y), pack_bf2(y.z, y.w));
-      }
-      c = c2;
-      sn = sn2;
     }
   }
   __syncthreads();
