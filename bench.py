@@ -226,6 +226,87 @@ def run_timeline(args):
     print(json.dumps(out), flush=True)
 
 
+def run_prepare(args):
+    """Cross-attention K/V preparation (register_prepare) of one predict, BASELINE configs[2]'s
+    prepare part: all layers' K/V from S source rows x 2048, one tcgen05 GEMM launch. Prints one
+    JSON line (not the headline metric)."""
+    from reki_megakernel_b200.prepare import RegisterPrepare
+    from reki_megakernel_b200.synthetic import ExpertDims, make_prepare_weights, make_source, rope_cos_sin
+    dims = ExpertDims()
+    pw = make_prepare_weights(dims, seed=0)
+    src_h = make_source(args.S, dims.src_dim, seed=0)
+    rp = RegisterPrepare(pw.to("cuda"))
+    src = src_h.to("cuda")
+    k, v = rp.run(src)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        rp.run(src, out=(k, v))
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        rp.run(src, out=(k, v))
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    for _ in range(args.warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    rp.check_device_error()
+    clocks = Clocks(0)
+    clocks.start()
+    time.sleep(0.3)
+    per = []
+    for _ in range(args.steps):
+        flush.fill_(1)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        g.replay()
+        b.record()
+        b.synchronize()
+        per.append(a.elapsed_time(b))
+    clk = clocks.stop()
+    rp.check_device_error()
+    ms = statistics.mean(per)
+    L, H, D, S = dims.L, dims.H, dims.src_dim, args.S
+    wbytes = L * 2 * H * D * 2
+    io_bytes = S * D * 2 + 2 * L * S * H * 2 + L * dims.HD * 4 + 2 * S * dims.HD * 4
+    flops = 2.0 * S * (L * 2 * H) * D
+    hbm, peak_kind = peaks()
+    achieved = (wbytes + io_bytes) / (ms * 1e-3) / 1e9
+    # CPU: the same projection + norm/RoPE in fp32 on the host cores (the restatement, no float64)
+    thr = len(os.sched_getaffinity(0))
+    torch.set_num_threads(thr)
+    c, sn = rope_cos_sin(torch.arange(S), dims.HD)
+    x = src_h.float()
+    wf = pw.wkv.float()
+    t0 = time.perf_counter()
+    reps = 0
+    while reps < 2 or time.perf_counter() - t0 < 5.0:
+        for l in range(L):
+            kk = (x @ wf[l, 0].T).reshape(S, dims.NH, dims.HD)
+            vv = x @ wf[l, 1].T
+            kk = kk * torch.rsqrt(kk.pow(2).mean(-1, keepdim=True) + pw.eps) * (1.0 + pw.kn[l])
+            rot = torch.cat([-kk[..., dims.HD // 2:], kk[..., :dims.HD // 2]], -1)
+            kk = (kk * c[:, None] + rot * sn[:, None]).to(torch.bfloat16)
+            vv = vv.to(torch.bfloat16)
+        reps += 1
+    cpu_ms = (time.perf_counter() - t0) / reps * 1e3
+    line = {
+        "metric": "register_prepare us per predict (cross-attention K/V of all layers)", "value": ms * 1e3,
+        "unit": "us", "higher_is_better": False, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "dtype": "bf16", "data": "synthetic (seeded N(0,0.02) projections, N(0,1)x0.5 source)",
+        "config": {"workload": f"K/V projection of S={S} source rows x {D} for {L} layers + K head RMSNorm + RoPE",
+                   "S": S, "src_dim": D, "layers": L, "l2": "256 MB written between timed steps (untimed)"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_kind": f"{peak_kind} (hbm copy, burst)", "algorithmic_bytes": wbytes + io_bytes},
+        "tensor_tflops": flops / (ms * 1e-3) / 1e12,
+        "gpu_launches": args.steps,
+        "clocks": clk,
+        "cpu_baseline": {"value": cpu_ms * 1e3, "unit": "us", "cores": thr, "kind": "port",
+                         "sample": f"{reps} full preparations, fp32 torch on the host"},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def episodes_of_rank(rank: int, batch: int) -> list[int]:
     """Global episode indices served by this rank: ranks own disjoint, consecutive blocks of
     `batch` episodes, each seeded by its index."""
@@ -400,14 +481,15 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--max-ref-steps", type=int, default=60)
     ap.add_argument("--timeline", action="store_true", help="per-stage critical path of one predict, no bench line")
+    ap.add_argument("--prepare", action="store_true", help="time register_prepare (cross-attention K/V), own JSON line")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    if args.timeline:
+    if args.timeline or args.prepare:
         if rank == 0:
-            run_timeline(args)
+            (run_timeline if args.timeline else run_prepare)(args)
         return
     if world > 1:
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")

@@ -38,8 +38,9 @@ typedef struct {
 } mkx_prep_dims;
 
 /* wkv: [L][2][H][src_dim] bf16 (K projection then V projection of each layer, row-major [out, in]);
- * kn: [L][HD] fp32 (K norm weight, scale = 1 + kn). Both are read in place by every run: they must
- * stay valid until mkx_prep_destroy. */
+ * kn: [L][HD] fp32 (K norm weight, scale = 1 + kn). Both are copied into the handle (W repacked into
+ * tile-contiguous, pre-swizzled blocks, L * 3 MB at src_dim = 2048); the caller may free them once
+ * this returns. Synchronises the device. */
 mkx_status mkx_prep_create(const mkx_prep_dims* dims, const uint16_t* wkv, const float* kn, int device,
                            mkx_prep_handle** out);
 

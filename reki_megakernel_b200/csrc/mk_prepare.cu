@@ -3,8 +3,10 @@
 //
 //   D[f, n] = sum_k Wkv[f, k] * src[n, k]      f over [L][K|V][768] (15,360 rows at REKI's sizes)
 //
-// One CTA per (128-feature tile, block of <= 256 tokens). Warp 0: TMA producer (128-byte swizzled
-// K-major tiles of W and src, 4-stage mbarrier ring). Warp 1: allocates 256 TMEM columns and issues
+// One CTA per (128-feature tile, block of <= 256 tokens). Warp 0: producer into an mbarrier ring of up
+// to 8 stages: the W tile as one contiguous 16 KB bulk copy from a copy of W packed at create time in
+// the 128-byte-swizzled K-major order the MMA reads (tile-contiguous, so HBM sees long bursts), the
+// source rows by TMA with the same swizzle. Warp 1: allocates 256 TMEM columns and issues
 // tcgen05.mma kind::f16 (M = 128, N = tokens, K = 16 per instruction, bf16 in, fp32 accumulate in
 // TMEM), committing each stage back to the producer. Warps 2-5 (one per TMEM lane quarter): read the
 // accumulator with tcgen05.ld, transpose it through shared memory (reusing the drained stage ring),
@@ -26,7 +28,8 @@ using namespace mkx;
 constexpr int BM = 128;             // output features per tile (UMMA M)
 constexpr int BK = 64;              // K elements per stage: one 128-byte swizzle row
 constexpr int MAXN = 256;           // tokens per tile (UMMA N)
-constexpr int STAGES = 4;
+constexpr int MAX_STAGES = 8;      // ring depth: as many stages as fit (weights in flight per SM)
+constexpr int SMEM_BUDGET = 227 * 1024;
 constexpr int NTHREADS = 192;       // warp 0 TMA, warp 1 TMEM + MMA, warps 2-5 epilogue
 constexpr int TMEM_COLS = 256;
 constexpr int TS = BM + 4;          // transposed tile: floats per token row (16-byte aligned rows)
@@ -35,7 +38,8 @@ constexpr int H = 768, NH = 12, HD = 64;
 constexpr int TILES_PER_LAYER = 2 * H / BM;  // 6 K tiles then 6 V tiles
 
 struct PrepParams {
-  int S, SP, ntok, L, ktiles;
+  int S, SP, ntok, L, ktiles, stages;
+  const uint16_t* wpk;  // packed W: [tile][kb][128 rows x 64] swizzled, 16 KB per (tile, kb)
   float eps;
   const float* kn;
   const float* cos;
@@ -110,19 +114,19 @@ __device__ __forceinline__ void record(const PrepParams& p, int code) { atomicCA
 extern __shared__ __align__(1024) char psmem[];
 
 __global__ void __launch_bounds__(NTHREADS, 1)
-    prep_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap ts,
-                const __grid_constant__ PrepParams p) {
+    prep_kernel(const __grid_constant__ CUtensorMap ts, const __grid_constant__ PrepParams p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x, tok0 = blockIdx.y * p.ntok;
   const int stage_bytes = A_BYTES + p.ntok * BK * 2;  // a multiple of 1024
   // every stage's A and B tile must start on a 1024-byte boundary (128-byte swizzle atoms): align the
   // ring inside the dynamic allocation, which is sized with 1 KB to spare
   char* ring = psmem + ((1024u - (smem_u32(psmem) & 1023u)) & 1023u);
+  const int STAGES = p.stages;
   uint64_t* bars = reinterpret_cast<uint64_t*>(ring + STAGES * stage_bytes);
   uint64_t* full = bars;
-  uint64_t* empty = bars + STAGES;
-  uint64_t* done = bars + 2 * STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 1);
+  uint64_t* empty = bars + MAX_STAGES;
+  uint64_t* done = bars + 2 * MAX_STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * MAX_STAGES + 1);
   int* consumed_slot = reinterpret_cast<int*>(tmem_slot + 1);
 
   if (threadIdx.x == 0) {
@@ -154,7 +158,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
       char* a = ring + s * stage_bytes;
       mbar_expect_tx(&full[s], (uint32_t)stage_bytes);
-      tma_load_2d(a, &tw, kb * BK, tile * BM, &full[s]);
+      bulk_g2s(a, p.wpk + ((size_t)tile * p.ktiles + kb) * (A_BYTES / 2), (uint32_t)A_BYTES, &full[s]);
       tma_load_2d(a + A_BYTES, &ts, kb * BK, tok0, &full[s]);
       issued = kb + 1;
     }
@@ -276,6 +280,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   }
 }
 
+// Packs W [rows][src_dim] into [tile][kb][128 x 64] blocks laid out as a 128-byte-swizzled K-major
+// tile (16-byte chunk c of row r at r * 128 + (c ^ (r % 8)) * 16): what a TMA load with 128-byte
+// swizzle would leave in shared memory, so a plain bulk copy of a block reproduces it.
+__global__ void prep_pack_kernel(const uint16_t* __restrict__ w, uint16_t* __restrict__ out, int tiles, int ktiles,
+                                 int src_dim) {
+  const long long total = (long long)tiles * ktiles * BM * 8;  // 16-byte chunks
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
+       e += (long long)gridDim.x * blockDim.x) {
+    const int c = (int)(e & 7), r = (int)((e >> 3) % BM);
+    const long long blk = e / (8 * BM);
+    const int kb = (int)(blk % ktiles), tile = (int)(blk / ktiles);
+    const uint4 v = *reinterpret_cast<const uint4*>(w + (size_t)(tile * BM + r) * src_dim + kb * BK + c * 8);
+    *reinterpret_cast<uint4*>(reinterpret_cast<char*>(out) + blk * A_BYTES + r * 128 + ((c ^ (r & 7)) << 4)) = v;
+  }
+}
+
 // ---------------------------------------------------------------------------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -312,9 +332,8 @@ static bool encode_bf16(CUtensorMap* m, const void* base, uint64_t rows, uint64_
 struct mkx_prep_handle {
   mkx_prep_dims d;
   int device;
-  const uint16_t* wkv;
-  const float* kn;
-  CUtensorMap tw;
+  uint16_t* wpk;  // packed W (owned)
+  float* kn;      // K norm weights (owned copy)
   int* status;
   unsigned long long timeout_ns;
   cudaStream_t last_stream;
@@ -336,13 +355,20 @@ extern "C" mkx_status mkx_prep_create(const mkx_prep_dims* dims, const uint16_t*
   memset(h, 0, sizeof(*h));
   h->d = d;
   h->device = device;
-  h->wkv = wkv;
-  h->kn = kn;
   h->timeout_ns = 2000000000ull;
-  if (!encode_bf16(&h->tw, wkv, (uint64_t)d.L * 2 * H, (uint64_t)d.src_dim, BM) ||
-      cudaMalloc(&h->status, sizeof(int)) != cudaSuccess || cudaMemset(h->status, 0, sizeof(int)) != cudaSuccess ||
-      cudaFuncSetAttribute(prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           STAGES * (A_BYTES + MAXN * BK * 2) + 1024 + 64 * 8) != cudaSuccess) {
+  const int tiles = d.L * TILES_PER_LAYER, ktiles = d.src_dim / BK;
+  const size_t wbytes = (size_t)tiles * ktiles * A_BYTES;
+  bool ok = cudaMalloc(&h->wpk, wbytes) == cudaSuccess && cudaMalloc(&h->kn, (size_t)d.L * HD * 4) == cudaSuccess &&
+            cudaMalloc(&h->status, sizeof(int)) == cudaSuccess && cudaMemset(h->status, 0, sizeof(int)) == cudaSuccess &&
+            cudaMemcpy(h->kn, kn, (size_t)d.L * HD * 4, cudaMemcpyDeviceToDevice) == cudaSuccess &&
+            cudaFuncSetAttribute(prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BUDGET) == cudaSuccess;
+  if (ok) {
+    prep_pack_kernel<<<1184, 256>>>(wkv, h->wpk, tiles, ktiles, d.src_dim);
+    ok = cudaGetLastError() == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess;
+  }
+  if (!ok) {
+    if (h->wpk) cudaFree(h->wpk);
+    if (h->kn) cudaFree(h->kn);
     if (h->status) cudaFree(h->status);
     delete h;
     return MKX_ERR_CUDA;
@@ -362,6 +388,14 @@ extern "C" mkx_status mkx_prep_run(mkx_prep_handle* h, const uint16_t* src, int 
   const int ntok = S >= MAXN ? MAXN : ((S + 15) / 16) * 16;
   CUtensorMap ts;
   if (!encode_bf16(&ts, src, (uint64_t)S, (uint64_t)h->d.src_dim, (uint32_t)ntok)) return MKX_ERR_CUDA;
+  // as many ring stages as fit next to the alignment slack and the barriers (the transposed
+  // accumulator tile reuses the ring; it always fits in 2 stages), at least 80 KB in total: at most
+  // 2 CTAs per SM, so their 2 x 256 TMEM columns always fit the SM's 512 and no allocation waits
+  const int stage_bytes = A_BYTES + ntok * BK * 2, slack = 1024 + 64 * 8;
+  int stages = (SMEM_BUDGET - slack) / stage_bytes;
+  if (stages > MAX_STAGES) stages = MAX_STAGES;
+  int smem = stages * stage_bytes + slack;
+  if (smem < 80 * 1024) smem = 80 * 1024;
   PrepParams p;
   memset(&p, 0, sizeof(p));
   p.S = S;
@@ -369,20 +403,18 @@ extern "C" mkx_status mkx_prep_run(mkx_prep_handle* h, const uint16_t* src, int 
   p.ntok = ntok;
   p.L = h->d.L;
   p.ktiles = h->d.src_dim / BK;
+  p.stages = stages;
   p.eps = h->d.eps;
   p.kn = h->kn;
+  p.wpk = h->wpk;
   p.cos = cos;
   p.sin = sin;
   p.k_out = k_out;
   p.v_out = v_out;
   p.status = h->status;
   p.timeout_ns = h->timeout_ns;
-  // ring + alignment slack + barriers, and at least 80 KB: at most 2 CTAs per SM, so their 2 x 256
-  // TMEM columns always fit the SM's 512 and no allocation waits for another CTA
-  int smem = STAGES * (A_BYTES + ntok * BK * 2) + 1024 + 64 * 8;
-  if (smem < 80 * 1024) smem = 80 * 1024;
   const dim3 grid(h->d.L * TILES_PER_LAYER, (S + ntok - 1) / ntok);
-  prep_kernel<<<grid, NTHREADS, smem, stream>>>(h->tw, ts, p);
+  prep_kernel<<<grid, NTHREADS, smem, stream>>>(ts, p);
   if (cudaGetLastError() != cudaSuccess) return MKX_ERR_CUDA;
   h->last_stream = stream;
   return MKX_OK;
@@ -399,6 +431,8 @@ extern "C" mkx_status mkx_prep_last_error(mkx_prep_handle* h, int* code) {
 extern "C" void mkx_prep_destroy(mkx_prep_handle* h) {
   if (!h) return;
   cudaSetDevice(h->device);
+  if (h->wpk) cudaFree(h->wpk);
+  if (h->kn) cudaFree(h->kn);
   if (h->status) cudaFree(h->status);
   delete h;
 }
