@@ -155,7 +155,7 @@ typedef struct {
  * dims->grid; 0 = one CTA per SM), the step inputs and x_out, all in memory it owns, plus an
  * optional device int err_out that receives the launch's error word (0 when every wait finished).
  * The kernel's scratch -- the exchange buffers and status words -- is a file-scope static device
- * array of 1,286,176 bytes, which every GPU that loads this library keeps until the process exits;
+ * array of 2,072,608 bytes, which every GPU that loads this library keeps until the process exits;
  * it holds I <= 3072 and T <= 16, and larger sizes return MKX_ERR_UNSUPPORTED with a message in
  * mkx_last_cuda_error(). Nothing in this call allocates. The first call on a device looks up the
  * array's device address and raises the kernel's shared-memory limit, so make that first call

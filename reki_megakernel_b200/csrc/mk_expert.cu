@@ -63,7 +63,13 @@ constexpr int NCOL = (H + NT - 1) / NT;   // in-projection columns per thread
 constexpr int TAIL_FLOATS = AO * H + H + 32;   // win rows 0..7 | bin | bout (padded)
 constexpr int MAX_STEP_TAGS = 4096;      // tag = seq * 4096 + instance + 1
 
-enum Buf { B_QKV = 0, B_Y, B_H2, B_QCA, B_YCA, B_H3, B_G, B_HOUT, B_X, NBUF };
+enum Buf { B_QKV = 0, B_Y, B_H2, B_QCA, B_YCA, B_H3, B_G, B_HOUT, B_X, B_DP, NBUF };
+// The down projection runs in two levels: the CTAs form NGRP groups; group j multiplies the g columns
+// [j I / NGRP, (j + 1) I / NGRP) by the matching K-slice of Wd for all H outputs (each CTA a run of
+// output columns) and publishes fp32 partial sums (B_DP: per token row, NGRP x H words of one fp32
+// each); the owner of an output column then adds the NGRP partials in group order.
+constexpr int NGRP = 4;
+constexpr int DPWORDS = NGRP * H;         // B_DP words per token row
 enum Slot { S_QKV = 0, S_O, S_QCA, S_OCA, S_GU, S_D, NSLOT };
 constexpr int BAR_MODS = NSLOT;          // mbarriers NSLOT, NSLOT + 1: modulation ring slots
 constexpr int NBAR = NSLOT + 2;
@@ -124,6 +130,7 @@ extern __shared__ __align__(1024) char g_smem[];
 
 struct Cta {
   int r0_qkv, R_qkv, c0, R_h, u0, R_gu;
+  int dgrp, d0, R_dp;  // down partials: group, first output column, output columns
   uint32_t tag0;
   int tid, warp, lane, cta, G;
   int stages;
@@ -187,7 +194,10 @@ __device__ __forceinline__ const uint16_t* slot_src(const Params& p, const Cta& 
     case S_QCA: return p.w[S_QCA] + (size_t)l * HH + (size_t)c.c0 * H;
     case S_OCA: return p.w[S_OCA] + (size_t)l * HH + (size_t)c.c0 * H;
     case S_GU: return p.w[S_GU] + (size_t)l * 2 * p.I * H + (size_t)2 * c.u0 * H;
-    default: return p.w[S_D] + (size_t)l * H * p.I + (size_t)c.c0 * p.I;
+    default: {
+      const int KS = p.I / NGRP;
+      return p.w[S_D] + (size_t)l * H * p.I + (size_t)c.dgrp * H * KS + (size_t)c.d0 * KS;
+    }
   }
 }
 
@@ -196,7 +206,7 @@ __device__ __forceinline__ uint32_t slot_bytes(const Params& p, const Cta& c, in
   switch (slot) {
     case S_QKV: return (uint32_t)c.R_qkv * H * 2;
     case S_GU: return (uint32_t)c.R_gu * H * 4;
-    case S_D: return (uint32_t)c.R_h * p.I * 2;
+    case S_D: return (uint32_t)c.R_dp * (p.I / NGRP) * 2;
     default: return (uint32_t)c.R_h * H * 2;
   }
 }
@@ -533,22 +543,24 @@ __device__ void epi_plain(const Params& p, const Cta& c, int R, int col0, u64* o
   }
 }
 
-// Gated residual out = bf16(res + bf16(acc) * gate) (src/mk_expert.py:162-172); gate in shared memory.
+// Gated residual out = bf16(res + bf16(acc) * gate) (src/mk_expert.py:162-172) of the column pair
+// c0 + 2 pp, token n; gate in shared memory.
 template <typename ModT>
-__device__ void epi_gated(const Params& p, const Cta& c, const ModT* gate, u64* out_rows, uint32_t tag,
-                          uint16_t* trace) {
+__device__ __forceinline__ void gated_pair_store(const Params& p, const Cta& c, const ModT* gate, u64* out_rows,
+                                                 uint32_t tag, uint16_t* trace, int pp, int n, float2 v) {
+  const float2 gv = mod2<ModT>(gate, c.c0 + 2 * pp);
+  const float a0 = round_bf(v.x), a1 = round_bf(v.y);
+  const float o0 = fmaf(a0, gv.x, cRes(p, c)[n * RESW + 2 * pp]);
+  const float o1 = fmaf(a1, gv.y, cRes(p, c)[n * RESW + 2 * pp + 1]);
+  const uint32_t pl = pack_bf2(o0, o1);
+  st_volatile(out_rows + (size_t)n * HWORDS + word_pos((c.c0 >> 1) + pp), make_word(tag, pl));
+  if (trace) *reinterpret_cast<uint32_t*>(trace + (size_t)n * H + c.c0 + 2 * pp) = pl;
+}
+template <typename ModT>
+__device__ void epi_gated(const Params& p, const Cta& c, const ModT* gate, u64* out_rows, uint32_t tag) {
   const int npairs = c.R_h >> 1, pp = c.tid % npairs, n = c.tid / npairs;
-  if (c.tid < npairs * p.T) {
-    const Split q = gemm_split(1, c.R_h);
-    const float2 gv = mod2<ModT>(gate, c.c0 + 2 * pp);
-    const float2 v = part_sum2(p, c, q, 0, pp, n);
-    const float a0 = round_bf(v.x), a1 = round_bf(v.y);
-    const float o0 = fmaf(a0, gv.x, cRes(p, c)[n * RESW + 2 * pp]);
-    const float o1 = fmaf(a1, gv.y, cRes(p, c)[n * RESW + 2 * pp + 1]);
-    const uint32_t pl = pack_bf2(o0, o1);
-    st_volatile(out_rows + (size_t)n * HWORDS + word_pos((c.c0 >> 1) + pp), make_word(tag, pl));
-    if (trace) *reinterpret_cast<uint32_t*>(trace + (size_t)n * H + c.c0 + 2 * pp) = pl;
-  }
+  if (c.tid < npairs * p.T)
+    gated_pair_store<ModT>(p, c, gate, out_rows, tag, nullptr, pp, n, part_sum2(p, c, gemm_split(1, c.R_h), 0, pp, n));
 }
 
 // g = bf16(silu(bf16(gate)) * bf16(up)) (src/mk_expert.py:403-413).
@@ -1004,29 +1016,162 @@ __device__ __forceinline__ int stage_norm_gemm(const Params& p, Cta& c, int whic
 }
 
 // GEMM stages fed straight from an exchange buffer, with a gated-residual epilogue.
-// which = 0: h2 = bf16(h + bf16(y @ Wo^T) * gate_sa); 1: h3 = bf16(h2 + bf16(y_ca @ Woca^T) * gate_ca);
-// 2: h = bf16(h3 + bf16(g @ Wd^T) * gate_mlp). q: the modulation block holding the gate.
+// which = 0: h2 = bf16(h + bf16(y @ Wo^T) * gate_sa); 1: h3 = bf16(h2 + bf16(y_ca @ Woca^T) * gate_ca).
+// q: the modulation block holding the gate.
 template <typename ModT>
 __device__ __forceinline__ int stage_words_gemm(const Params& p, Cta& c, int which, int gi, int q) {
   const int par = gi & 1;
   const uint32_t tag = c.tag0 + (uint32_t)gi;
   u64* const* xb = p.xb;
-  const int slot = which == 0 ? S_O : (which == 1 ? S_OCA : S_D);
-  const int K = which == 2 ? p.I : H;
-  const u64* rows = which == 2 ? xb[B_G] + (size_t)par * TP * (p.I >> 1)
-                               : xb[which == 0 ? B_Y : B_YCA] + (size_t)par * TP * HWORDS;
+  const int slot = which == 0 ? S_O : S_OCA;
+  const u64* rows = xb[which == 0 ? B_Y : B_YCA] + (size_t)par * TP * HWORDS;
   __syncthreads();
   int fail = !wait_bar(p, c, slot);
   if (__syncthreads_or(fail)) return 1;
   consumed(p, c, slot);
   MKX_TRACE(0);
-  fail = mma_from_words(p, c, cSlot(p, c, slot), c.R_h, K, rows, tag, ST_O + 3 * which);
+  fail = mma_from_words(p, c, cSlot(p, c, slot), c.R_h, H, rows, tag, ST_O + 3 * which);
   if (__syncthreads_or(fail)) return 1;
   MKX_TRACE(1);
   if (c.tid == ISSUER && gi + 1 < p.n_steps * p.L) issue_slot(p, c, slot, (gi + 1) % p.L);
-  u64* out = xb[which == 0 ? B_H2 : (which == 1 ? B_H3 : B_HOUT)] + (size_t)par * TP * HWORDS;
-  epi_gated<ModT>(p, c, mods_slot<ModT>(p, c, q) + 2 * H, out, tag,
-                  (which == 2 && p.trace_h) ? p.trace_h + (size_t)gi * p.T * H : nullptr);
+  u64* out = xb[which == 0 ? B_H2 : B_H3] + (size_t)par * TP * HWORDS;
+  epi_gated<ModT>(p, c, mods_slot<ModT>(p, c, q) + 2 * H, out, tag);
+  MKX_TRACE(5);
+  __syncthreads();
+  MKX_TRACE(6);
+  if (c.tid == ISSUER) issue_mods<ModT>(p, c, q + 2);  // this block's last use
+  return 0;
+}
+
+// Down projection, level 1 (src/mk_expert.py:416-419 with K split over the NGRP groups): this CTA's
+// R_dp output columns from d0 over its group's K-slice of g, polled straight from B_G (a warp's
+// whole K range in flight at once), up to two m-tiles, K split over the 8 warps. Partials to P as
+// [m-tile][warp] blocks. Returns nonzero on a failed wait.
+__device__ int down_partial(const Params& p, Cta& c, int par, uint32_t tag) {
+  constexpr int CH = 6;
+  const int RW = p.I >> 1, KB = (p.I / NGRP) >> 4, R = c.R_dp;
+  const int g = c.lane >> 2, cc = c.lane & 3;
+  const int kb0 = c.warp * KB / NW, kb1 = (c.warp + 1) * KB / NW;
+  const bool v0 = g < p.T, v1 = (8 + g) < p.T, two = p.T > 8, m1 = R > 16;
+  const u64* row0 = p.xb[B_G] + (size_t)par * TP * RW + (size_t)g * RW + 2 * cc + (size_t)c.dgrp * KB * 8;
+  const size_t d1off = (size_t)8 * RW;  // token row 8 + g
+  const char* A = cSlot(p, c, S_D) + cc * 8;
+  const bool va0 = g < R, vb0 = g + 8 < R, va1 = g + 16 < R, vb1 = g + 24 < R;
+  float d[2][2][4] = {};  // [m-tile][token rows 0-7 / 8-15][fragment]
+  Waiter wt(p.status, p.timeout_ns);
+  int rc = 0;
+  for (int kc = kb0; kc < kb1; kc += CH) {
+    u64 w0[2 * CH], w1[2 * CH];
+    uint32_t valid = 0;
+#pragma unroll
+    for (int i = 0; i < CH; ++i)
+      if (kc + i < kb1) valid |= ((v0 ? 1u : 0u) | (v1 ? 2u : 0u)) << (2 * i);
+    const u64* base = row0 + (size_t)kc * 8;
+    auto addr = [base, d1off](int i) { return base + (i >> 1) * 8 + ((i & 1) ? d1off : 0); };
+    issue_pairs<2 * CH>(addr, w0, w1, valid, tag);
+    const int r = complete_pairs<2 * CH>(addr, w0, w1, tag, wt);
+    if (__any_sync(0xffffffffu, r != 0)) {  // keep the warp converged for mma.sync
+      rc = r ? r : 2;
+      break;
+    }
+#pragma unroll
+    for (int i = 0; i < CH; ++i) {
+      if (kc + i < kb1) {
+        const char* blk = A + (size_t)(kc + i) * R * 32;
+        const uint32_t b0 = payload_of(w0[2 * i]), b1 = payload_of(w1[2 * i]);
+        const uint32_t e0 = payload_of(w0[2 * i + 1]), e1 = payload_of(w1[2 * i + 1]);
+        {
+          const uint2 a = va0 ? lds64(blk + g * 32) : make_uint2(0u, 0u);
+          const uint2 b = vb0 ? lds64(blk + (g + 8) * 32) : make_uint2(0u, 0u);
+          mma_bf16(d[0][0], a.x, b.x, a.y, b.y, b0, b1);
+          if (two) mma_bf16(d[0][1], a.x, b.x, a.y, b.y, e0, e1);
+        }
+        if (m1) {
+          const uint2 a = va1 ? lds64(blk + (g + 16) * 32) : make_uint2(0u, 0u);
+          const uint2 b = vb1 ? lds64(blk + (g + 24) * 32) : make_uint2(0u, 0u);
+          mma_bf16(d[1][0], a.x, b.x, a.y, b.y, b0, b1);
+          if (two) mma_bf16(d[1][1], a.x, b.x, a.y, b.y, e0, e1);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt) {
+    float* P = cP(p, c) + (mt * NW + c.warp) * PM;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      P[(8 * h + 2 * cc) * PSTR + g] = d[mt][h][0];
+      P[(8 * h + 2 * cc + 1) * PSTR + g] = d[mt][h][1];
+      P[(8 * h + 2 * cc) * PSTR + g + 8] = d[mt][h][2];
+      P[(8 * h + 2 * cc + 1) * PSTR + g + 8] = d[mt][h][3];
+    }
+  }
+  return fail_code(p, c, rc, ST_DOWN);
+}
+
+// Down projection stage: level 1 (partials of the group's K-slice to B_DP), then level 2: the
+// NGRP partials of this CTA's columns [c0, c0 + R_h) added in group order, and the gated residual
+// h = bf16(h3 + bf16(g @ Wd^T) * gate_mlp) to B_HOUT. q: the MLP modulation block.
+template <typename ModT>
+__device__ __forceinline__ int stage_down(const Params& p, Cta& c, int gi, int q) {
+  const int par = gi & 1;
+  const uint32_t tag = c.tag0 + (uint32_t)gi;
+  __syncthreads();
+  int fail = !wait_bar(p, c, S_D);
+  if (__syncthreads_or(fail)) return 1;
+  consumed(p, c, S_D);
+  MKX_TRACE(0);
+  fail = down_partial(p, c, par, tag);
+  if (__syncthreads_or(fail)) return 1;
+  MKX_TRACE(1);
+  if (c.tid == ISSUER && gi + 1 < p.n_steps * p.L) issue_slot(p, c, S_D, (gi + 1) % p.L);
+  {  // partial sums (token n, column r): columns fastest, consecutive lanes store consecutive words
+    u64* dp = p.xb[B_DP] + (size_t)par * TP * DPWORDS + (size_t)c.dgrp * H + c.d0;
+    for (int e = c.tid; e < p.T * c.R_dp; e += NT) {
+      const int n = e / c.R_dp, r = e - n * c.R_dp;
+      const float* P = cP(p, c) + (r >> 4) * NW * PM + n * PSTR + (r & 15);
+      float v[NW];
+#pragma unroll
+      for (int k = 0; k < NW; ++k) v[k] = P[k * PM];
+#pragma unroll
+      for (int w = NW / 2; w >= 1; w >>= 1)
+#pragma unroll
+        for (int k = 0; k < w; ++k) v[k] += v[k + w];
+      st_volatile(dp + (size_t)n * DPWORDS + r, make_word(tag, __float_as_uint(v[0])));
+    }
+  }
+  MKX_TRACE(2);
+  __syncthreads();  // P is reused below
+  float* S = cP(p, c);  // [NGRP][TP][RESW] partials of this CTA's columns
+  {
+    const u64* src = p.xb[B_DP] + (size_t)par * TP * DPWORDS + c.c0;
+    const int per = p.T * c.R_h;
+    Waiter wt(p.status, p.timeout_ns);
+    int r = 0;
+    for (int e = c.tid; e < NGRP * per && r == 0; e += NT) {
+      const int j = e / per, rem = e - j * per, n = rem / c.R_h, col = rem - n * c.R_h;
+      u64 w = 0;
+      r = poll_word(src + (size_t)n * DPWORDS + (size_t)j * H + col, w, tag, wt);
+      S[(j * TP + n) * RESW + col] = __uint_as_float(payload_of(w));
+    }
+    fail = fail_code(p, c, r, ST_DOWN);
+  }
+  if (__syncthreads_or(fail)) return 1;
+  MKX_TRACE(3);
+  {
+    const int npairs = c.R_h >> 1, pp = c.tid % npairs, n = c.tid / npairs;
+    if (c.tid < npairs * p.T) {
+      float2 v = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < NGRP; ++j) {
+        const float2 t = *reinterpret_cast<const float2*>(S + (j * TP + n) * RESW + 2 * pp);
+        v.x += t.x;
+        v.y += t.y;
+      }
+      gated_pair_store<ModT>(p, c, mods_slot<ModT>(p, c, q) + 2 * H, p.xb[B_HOUT] + (size_t)par * TP * HWORDS, tag,
+                             p.trace_h ? p.trace_h + (size_t)gi * p.T * H : nullptr, pp, n, v);
+    }
+  }
   MKX_TRACE(5);
   __syncthreads();
   MKX_TRACE(6);
@@ -1094,6 +1239,11 @@ __global__ void __launch_bounds__(NT, 1) expert_kernel(const __grid_constant__ P
     c.c0 = 2 * lo; c.R_h = 2 * (hi - lo);
     lo = part_lo(i, p.I / 2, G); hi = part_lo(i + 1, p.I / 2, G);
     c.u0 = 2 * lo; c.R_gu = 2 * (hi - lo);
+    int j = 0;
+    while (j + 1 < NGRP && i >= part_lo(j + 1, G, NGRP)) ++j;
+    const int g0 = part_lo(j, G, NGRP), gn = part_lo(j + 1, G, NGRP) - g0;
+    lo = part_lo(i - g0, H / 2, gn); hi = part_lo(i - g0 + 1, H / 2, gn);
+    c.dgrp = j; c.d0 = 2 * lo; c.R_dp = 2 * (hi - lo);
   }
   if (p.prof != nullptr && c.tid == 0) p.prof[(size_t)c.cta * (2 + p.n_steps * (8 * p.L + 1))] = globaltimer();
   const uint32_t seq = (uint32_t)ld_volatile_i32(p.status + 1);
@@ -1142,8 +1292,10 @@ __global__ void __launch_bounds__(NT, 1) expert_kernel(const __grid_constant__ P
           rc = stage_norm_gemm<ModT>(p, c, st / 3, gi, l, q_sa + st / 3);
         } else if (st == 1 || st == 4) {
           rc = stage_attention(p, c, st == 1, gi, l);
-        } else {  // st 2, 5, 7
-          const int which = st == 2 ? 0 : (st == 5 ? 1 : 2);
+        } else if (st == 7) {
+          rc = stage_down<ModT>(p, c, gi, q_sa + 2);
+        } else {  // st 2, 5
+          const int which = st == 2 ? 0 : 1;
           rc = stage_words_gemm<ModT>(p, c, which, gi, q_sa + which);
         }
         if (rc) goto drain;
@@ -1215,6 +1367,29 @@ __global__ void pack_kernel(const uint16_t* __restrict__ src0, const uint16_t* _
   }
 }
 
+// Packs Wd [L, H, I] for the two-level down projection: layer block l, then group j's block of
+// all H rows over K-slice j (I / NGRP columns), inside which CTA t of the group (Gj CTAs) stores its
+// R output rows from r0 (pairs split like every other matrix, over Gj) as [KS / 16][R][16] with the
+// A-fragment order of each 16-column block.
+__global__ void pack_down_kernel(const uint16_t* __restrict__ src, uint16_t* dst, int L, int I, int G) {
+  const long long total = (long long)L * H * I;
+  const int KS = I / NGRP;
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total; e += (long long)gridDim.x * blockDim.x) {
+    const int k = (int)(e % I);
+    const long long rest = e / I;
+    const int n = (int)(rest % H);
+    const int l = (int)(rest / H);
+    const int j = k / KS, kl = k - j * KS;
+    const int gn = part_lo(j + 1, G, NGRP) - part_lo(j, G, NGRP);
+    const int t = owner_of_pair(n >> 1, H / 2, gn);
+    const int r0 = 2 * part_lo(t, H / 2, gn);
+    const int R = 2 * part_lo(t + 1, H / 2, gn) - r0;
+    const long long d = (long long)l * H * I + (long long)j * H * KS + (long long)r0 * KS + (long long)(kl >> 4) * R * 16 +
+                        (long long)(n - r0) * 16 + perm16(kl & 15);
+    dst[d] = src[e];
+  }
+}
+
 __global__ void norm_kernel(const uint16_t* qn, const uint16_t* kn, const uint16_t* qcan, float* out, int L) {
   const int e = blockIdx.x * blockDim.x + threadIdx.x;
   if (e >= 3 * L * HD) return;
@@ -1267,7 +1442,7 @@ static void* halloc(mkx_handle* h, size_t bytes, cudaError_t* err) {
 struct Layout {
   int s_slot[NSLOT];
   int s_x, s_p, s_mods, s_xs, s_res, s_red, s_bar, s_cnt, total;
-  int max_rows_qkv, max_rows_h, max_rows_gu;
+  int max_rows_qkv, max_rows_h, max_rows_gu, max_rows_dp;
 };
 
 static int max_part(int P, int G) {
@@ -1292,6 +1467,11 @@ static Layout make_layout(int I, int G) {
   ly.max_rows_qkv = 2 * max_part(3 * H / 2, G);
   ly.max_rows_h = 2 * max_part(H / 2, G);
   ly.max_rows_gu = 2 * max_part(I / 2, G);
+  ly.max_rows_dp = 0;
+  for (int j = 0; j < NGRP; ++j) {
+    const int r = 2 * max_part(H / 2, part_lo(j + 1, G, NGRP) - part_lo(j, G, NGRP));
+    if (r > ly.max_rows_dp) ly.max_rows_dp = r;
+  }
   int off = 0;
   auto take = [&](int bytes) {
     const int o = off;
@@ -1303,10 +1483,10 @@ static Layout make_layout(int I, int G) {
   ly.s_slot[S_QCA] = take(ly.max_rows_h * H * 2);
   ly.s_slot[S_OCA] = take(ly.max_rows_h * H * 2);
   ly.s_slot[S_GU] = take(ly.max_rows_gu * H * 4);
-  ly.s_slot[S_D] = take(ly.max_rows_h * I * 2);
+  ly.s_slot[S_D] = take(ly.max_rows_dp * (I / NGRP) * 2);
   ly.s_x = take(TP * XS * 2);
   constexpr int attn_floats = NW * 64 + NW;  // attention output reduction: per-warp o and den
-  ly.s_p = take((attn_floats > NW * PM ? attn_floats : NW * PM) * 4);
+  ly.s_p = take((attn_floats > 2 * NW * PM ? attn_floats : 2 * NW * PM) * 4);  // down: two m-tiles of partials
   ly.s_mods = take(2 * 3 * H * 4);  // sized for fp32 modulations
   ly.s_xs = take(TP * 32 * 4);
   ly.s_res = take(TP * RESW * 4);
@@ -1343,7 +1523,9 @@ extern "C" mkx_status mkx_create(const mkx_dims* dims, const mkx_weights* w, int
   const Layout ly = make_layout(d.I, G);
   // one epilogue element (column pair, action row) per thread; this also keeps every matrix at <= 32
   // rows per CTA, the bound gemm_split assumes
-  if (ly.max_rows_qkv / 2 * TP > NT || ly.max_rows_h > RESW || ly.max_rows_gu / 2 * TP > NT) return MKX_ERR_RESOURCES;
+  // and the down partials at <= two m-tiles per CTA
+  if (ly.max_rows_qkv / 2 * TP > NT || ly.max_rows_h > RESW || ly.max_rows_gu / 2 * TP > NT || ly.max_rows_dp > 32)
+    return MKX_ERR_RESOURCES;
   if (ly.total > smem_optin) return MKX_ERR_RESOURCES;
 
   mkx_handle* h = new (std::nothrow) mkx_handle();
@@ -1367,7 +1549,7 @@ extern "C" mkx_status mkx_create(const mkx_dims* dims, const mkx_weights* w, int
   float* nrm = (float*)halloc(h, (size_t)3 * L * HD * 4, &err);
   float* tailw = err == cudaSuccess ? (float*)halloc(h, TAIL_FLOATS * 4, &err) : nullptr;
   float* wout = err == cudaSuccess ? (float*)halloc(h, (size_t)A * H * 4, &err) : nullptr;
-  const int rw[NBUF] = {QKVWORDS, HWORDS, HWORDS, HWORDS, HWORDS, HWORDS, I / 2, HWORDS, XWORDS};
+  const int rw[NBUF] = {QKVWORDS, HWORDS, HWORDS, HWORDS, HWORDS, HWORDS, I / 2, HWORDS, XWORDS, DPWORDS};
   size_t xwords = 0;
   for (int b = 0; b < NBUF; ++b) xwords += (size_t)2 * TP * rw[b];
   u64* xbase = err == cudaSuccess ? (u64*)halloc(h, xwords * 8, &err) : nullptr;
@@ -1382,7 +1564,7 @@ extern "C" mkx_status mkx_create(const mkx_dims* dims, const mkx_weights* w, int
   pack_kernel<<<blocks, 256, 0, st>>>(w->wqca, nullptr, wp[S_QCA], L, H, H, G, 1);
   pack_kernel<<<blocks, 256, 0, st>>>(w->woca, nullptr, wp[S_OCA], L, H, H, G, 1);
   pack_kernel<<<blocks, 256, 0, st>>>(w->wg, w->wu, wp[S_GU], L, I, H, G, 2);
-  pack_kernel<<<blocks, 256, 0, st>>>(w->wd, nullptr, wp[S_D], L, H, I, G, 1);
+  pack_down_kernel<<<blocks, 256, 0, st>>>(w->wd, wp[S_D], L, I, G);
   norm_kernel<<<(3 * L * HD + 255) / 256, 256, 0, st>>>(w->qn, w->kn, w->qcan, nrm, L);
   // tail weights: win rows 0..7 | bin | bout (padded to 32); wout keeps all A rows
   cudaMemsetAsync(tailw, 0, TAIL_FLOATS * 4, st);
@@ -1567,8 +1749,8 @@ extern "C" void mkx_destroy(mkx_handle* h) {
 namespace mkx {
 constexpr int STATIC_MAX_I = 3072;
 // exchange words of every buffer, both parities, TP rows, at the largest I; then 8 status ints
-constexpr size_t STATIC_XWORDS = (size_t)2 * TP * (QKVWORDS + 6 * HWORDS + STATIC_MAX_I / 2 + XWORDS);
-constexpr size_t STATIC_WORDS = STATIC_XWORDS + 4;  // 1,286,176 bytes
+constexpr size_t STATIC_XWORDS = (size_t)2 * TP * (QKVWORDS + 6 * HWORDS + STATIC_MAX_I / 2 + XWORDS + DPWORDS);
+constexpr size_t STATIC_WORDS = STATIC_XWORDS + 4;  // 2,072,608 bytes
 static __device__ __align__(256) u64 g_static_scratch[STATIC_WORDS];
 }  // namespace mkx
 
@@ -1643,7 +1825,7 @@ extern "C" mkx_status mkx_run_static(const mkx_dims* dims, const mkx_packed_weig
   const int G = d.grid > 0 ? d.grid : sd->sms;
   if (G < d.A || G < TP || G > H / 2 || G > sd->sms || min_part(d.I / 2, G) < 1) return MKX_ERR_RESOURCES;
   const Layout ly = make_layout(d.I, G);
-  if (ly.max_rows_qkv / 2 * TP > NT || ly.max_rows_h > RESW || ly.max_rows_gu / 2 * TP > NT ||
+  if (ly.max_rows_qkv / 2 * TP > NT || ly.max_rows_h > RESW || ly.max_rows_gu / 2 * TP > NT || ly.max_rows_dp > 32 ||
       ly.total > sd->smem_optin)
     return MKX_ERR_RESOURCES;
 
@@ -1653,7 +1835,7 @@ extern "C" mkx_status mkx_run_static(const mkx_dims* dims, const mkx_packed_weig
   p.nrm = w->nrm;
   p.tailw = w->tailw;
   p.wout = w->wout;
-  const int rw[NBUF] = {QKVWORDS, HWORDS, HWORDS, HWORDS, HWORDS, HWORDS, d.I / 2, HWORDS, XWORDS};
+  const int rw[NBUF] = {QKVWORDS, HWORDS, HWORDS, HWORDS, HWORDS, HWORDS, d.I / 2, HWORDS, XWORDS, DPWORDS};
   u64* xp = sd->scratch;
   for (int b = 0; b < NBUF; ++b) {
     p.xb[b] = xp;
