@@ -20,6 +20,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -224,6 +225,82 @@ def run_timeline(args):
            "predict_us": round(statistics.median(total), 1), "predicts": len(total),
            "config": "REKI expert steps 2-10, T=10, S=160, 64 memory rows, batch 1"}
     print(json.dumps(out), flush=True)
+
+
+def run_mods(args):
+    """Per-step modulation rows of one predict (BASELINE configs[2]'s modulation part): N = 10 rows of
+    MODW = 70,656 from the conditioning network, two launches (conditioning + HBM-bound projection).
+    Prints one JSON line (not the headline metric)."""
+    from reki_megakernel_b200.modulations import StepModulations
+    from reki_megakernel_b200.synthetic import ExpertDims, make_modulation_weights, make_state
+    dims = ExpertDims()
+    N = 10
+    w = make_modulation_weights(dims, seed=0)
+    st_h = make_state(w.sdim, seed=0)
+    sm = StepModulations(w.to("cuda"))
+    st = st_h.to("cuda")
+    mods, dt = sm(N, st)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        sm(N, st, out=(mods, dt))
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        sm(N, st, out=(mods, dt))
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    for _ in range(args.warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    clocks = Clocks(0)
+    clocks.start()
+    time.sleep(0.3)
+    per = []
+    for _ in range(args.steps):
+        flush.fill_(1)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        g.replay()
+        b.record()
+        b.synchronize()
+        per.append(a.elapsed_time(b))
+    clk = clocks.stop()
+    ms = statistics.mean(per)
+    MODW, H = dims.MODW, dims.H
+    wbytes = MODW * H * 2 + MODW * 4 + H * (w.tdim + w.sdim) * 4
+    io_bytes = N * MODW * 2
+    hbm, peak_kind = peaks()
+    achieved = (wbytes + io_bytes) / (ms * 1e-3) / 1e9
+    # CPU: the same network in fp32 on the host cores (bf16 weights widened once, outside the timing)
+    thr = len(os.sched_getaffinity(0))
+    torch.set_num_threads(thr)
+    wm = w.w_m.float()
+    t0 = time.perf_counter()
+    reps = 0
+    while reps < 2 or time.perf_counter() - t0 < 5.0:
+        half = w.tdim // 2
+        t = 1.0 - torch.arange(N, dtype=torch.float32) / N
+        f = torch.exp(-math.log(10000.0) * torch.arange(half, dtype=torch.float32) / half)
+        ang = 1000.0 * t[:, None] * f[None, :]
+        e = 8.0 * (torch.cat([ang.cos(), ang.sin()], 1) @ w.w_t.T + st_h[None, :] @ w.w_s.T)
+        a = torch.nn.functional.silu(e).to(torch.bfloat16).float()
+        (a @ wm.T + w.b_m).to(torch.bfloat16)
+        reps += 1
+    cpu_ms = (time.perf_counter() - t0) / reps * 1e3
+    line = {
+        "metric": "step modulations us per predict (AdaRMS rows of all layers and steps)", "value": ms * 1e3,
+        "unit": "us", "higher_is_better": False, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "dtype": "bf16", "data": "synthetic (seeded N(0,0.02) weights, U(-1,1) state)",
+        "config": {"workload": f"{N} steps x MODW={MODW} modulation rows (projection {MODW}x{H} bf16)",
+                   "N": N, "MODW": MODW, "l2": "256 MB written between timed steps (untimed); W_m 108.5 MB"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_kind": f"{peak_kind} (hbm copy, burst)", "algorithmic_bytes": wbytes + io_bytes},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clk,
+        "cpu_baseline": {"value": cpu_ms * 1e3, "unit": "us", "cores": thr, "kind": "port",
+                         "sample": f"{reps} full modulation computations, fp32 torch on the host"},
+    }
+    print(json.dumps(line), flush=True)
 
 
 def run_prepare(args):
@@ -482,14 +559,15 @@ def main():
     ap.add_argument("--max-ref-steps", type=int, default=60)
     ap.add_argument("--timeline", action="store_true", help="per-stage critical path of one predict, no bench line")
     ap.add_argument("--prepare", action="store_true", help="time register_prepare (cross-attention K/V), own JSON line")
+    ap.add_argument("--mods", action="store_true", help="time the per-step modulation rows (_step_modulations), own JSON line")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    if args.timeline or args.prepare:
+    if args.timeline or args.prepare or args.mods:
         if rank == 0:
-            (run_timeline if args.timeline else run_prepare)(args)
+            (run_timeline if args.timeline else run_prepare if args.prepare else run_mods)(args)
         return
     if world > 1:
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")

@@ -1,4 +1,5 @@
-"""ctypes binding of ``libmkx.so`` (declarations in ``include/mkx.h`` and ``include/mkx_prepare.h``).
+"""ctypes binding of ``libmkx.so`` (declarations in ``include/mkx.h``, ``include/mkx_prepare.h`` and
+``include/mkx_mods.h``).
 
 The library is built in-tree by ``reki_megakernel_b200.build``. There is no fallback: if the
 library is missing or does not load, importing this module raises.
@@ -49,6 +50,10 @@ class PrepDims(C.Structure):
                 ("eps", C.c_float)]
 
 
+class ModsDims(C.Structure):
+    _fields_ = [("H", C.c_int), ("L", C.c_int), ("tdim", C.c_int), ("sdim", C.c_int)]
+
+
 SIGNATURES = {
     "mkx_create": (C.c_int, [C.POINTER(Dims), C.POINTER(Weights), C.c_int, C.POINTER(P)]),
     "mkx_run": (C.c_int, [P, C.POINTER(StepInputs), P]),
@@ -65,6 +70,11 @@ SIGNATURES = {
     "mkx_prep_run": (C.c_int, [P, P, C.c_int, P, P, P, P, C.c_int, P]),
     "mkx_prep_last_error": (C.c_int, [P, C.POINTER(C.c_int)]),
     "mkx_prep_destroy": (None, [P]),
+    "mkx_mods_create": (C.c_int, [C.POINTER(ModsDims), P, P, P, P, C.c_int, C.POINTER(P)]),
+    "mkx_mods_run": (C.c_int, [P, C.c_int, P, P, P, P]),
+    "mkx_mods_width": (C.c_int, [P]),
+    "mkx_mods_input": (C.c_int, [P, P, P]),
+    "mkx_mods_destroy": (None, [P]),
 }
 
 _LIB = None

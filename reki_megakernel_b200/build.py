@@ -16,8 +16,9 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 LIB = PKG / "libmkx.so"
-SOURCES = [PKG / "csrc" / "mk_expert.cu", PKG / "csrc" / "mk_prepare.cu"]
-HEADERS = [PKG / "csrc" / "mkx_device.cuh", ROOT / "include" / "mkx.h", ROOT / "include" / "mkx_prepare.h"]
+SOURCES = [PKG / "csrc" / "mk_expert.cu", PKG / "csrc" / "mk_prepare.cu", PKG / "csrc" / "mk_mods.cu"]
+HEADERS = [PKG / "csrc" / "mkx_device.cuh", ROOT / "include" / "mkx.h", ROOT / "include" / "mkx_prepare.h",
+           ROOT / "include" / "mkx_mods.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -226,6 +226,48 @@ def make_source(S: int, src_dim: int = 2048, seed: int = 0) -> torch.Tensor:
     return (torch.randn((S, src_dim), generator=g) * 0.5).to(torch.bfloat16)
 
 
+@dataclass
+class ModulationWeights:
+    """Weights of the restated per-step modulation network (the GPU ``StepModulations``): timestep
+    embedding projection w_t [H, tdim] fp32, state projection w_s [H, sdim] fp32, the modulation
+    projection w_m [MODW, H] bf16 and its bias b_m [MODW] fp32."""
+    dims: ExpertDims
+    w_t: torch.Tensor
+    w_s: torch.Tensor
+    w_m: torch.Tensor
+    b_m: torch.Tensor
+
+    @property
+    def tdim(self) -> int:
+        return self.w_t.shape[1]
+
+    @property
+    def sdim(self) -> int:
+        return self.w_s.shape[1]
+
+    def to(self, device) -> "ModulationWeights":
+        return ModulationWeights(self.dims, self.w_t.to(device), self.w_s.to(device), self.w_m.to(device),
+                                 self.b_m.to(device))
+
+
+def make_modulation_weights(dims: ExpertDims = ExpertDims(), seed: int = 0, tdim: int = 256,
+                            sdim: int = 7) -> ModulationWeights:
+    """Seeded N(0, 0.02) weights of the modulation network (w_m rounded to bf16)."""
+    g = torch.Generator().manual_seed(seed + 29)
+    H = dims.H
+    w_t = torch.randn((H, tdim), generator=g) * 0.02
+    w_s = torch.randn((H, sdim), generator=g) * 0.02
+    w_m = (torch.randn((dims.MODW, H), generator=g) * 0.02).to(torch.bfloat16)
+    b_m = torch.randn((dims.MODW,), generator=g) * 0.02
+    return ModulationWeights(dims, w_t, w_s, w_m, b_m)
+
+
+def make_state(sdim: int = 7, seed: int = 0) -> torch.Tensor:
+    """Proprio state [sdim] fp32, U(-1, 1)."""
+    g = torch.Generator().manual_seed(seed + 31)
+    return torch.rand((sdim,), generator=g) * 2.0 - 1.0
+
+
 def make_inputs(dims: ExpertDims = ExpertDims(), *, B: int = 1, T: int = 10, n_steps: int = 9,
                 frame_slots: int = 3, frames_valid: int = 2, regs_per_frame: int = 32, S: int = 160,
                 SP: int | None = None, action_dim: int = 7, dt: float = 0.1, seed: int = 0,

@@ -97,3 +97,19 @@ def test_prepare_arguments_are_rejected_without_a_device():
     assert lib.mkx_prep_run(None, None, 0, None, None, None, None, 0, None) == _lib.MKX_ERR_INVALID_ARG
     assert lib.mkx_prep_last_error(None, None) == _lib.MKX_ERR_INVALID_ARG
     lib.mkx_prep_destroy(None)
+
+
+def test_modulation_arguments_are_rejected_without_a_device():
+    from reki_megakernel_b200 import _lib
+    lib = _lib.load()
+    h = C.c_void_p()
+    assert lib.mkx_mods_create(None, None, None, None, None, 0, C.byref(h)) == _lib.MKX_ERR_INVALID_ARG
+    for d in (_lib.ModsDims(H=1024, L=10, tdim=256, sdim=7),    # width the kernels are not built for
+              _lib.ModsDims(H=768, L=10, tdim=100, sdim=7),     # embedding width not a multiple of 64
+              _lib.ModsDims(H=768, L=10, tdim=256, sdim=65),    # state wider than 64
+              _lib.ModsDims(H=768, L=0, tdim=256, sdim=7)):
+        assert lib.mkx_mods_create(C.byref(d), 16, 16, 16, 16, 0, C.byref(h)) == _lib.MKX_ERR_UNSUPPORTED
+    assert lib.mkx_mods_run(None, 10, None, None, None, None) == _lib.MKX_ERR_INVALID_ARG
+    assert lib.mkx_mods_width(None) == 0
+    assert lib.mkx_mods_input(None, None, None) == _lib.MKX_ERR_INVALID_ARG
+    lib.mkx_mods_destroy(None)
