@@ -48,9 +48,14 @@ mkx_status mkx_mods_create(const mkx_mods_dims* dims, const float* w_t, const fl
 
 /* Modulation rows of an N-step predict: state [sdim] fp32 (device); mods_out [N][MODW] bf16, rows
  * contiguous (row stride MODW); dt_out: one fp32 (device), receives 1 / N. 1 <= N <= 16.
- * Asynchronous on `stream` (two kernel launches, no waits); graph-capturable. */
+ * Asynchronous on `stream` (two kernel launches, the second a programmatic dependent of the first;
+ * no spin waits); graph-capturable. */
 mkx_status mkx_mods_run(mkx_mods_handle* h, int N, const float* state, uint16_t* mods_out, float* dt_out,
                         cudaStream_t stream);
+
+/* Reads the device error word (synchronises the handle's last stream first): 0 = no error. The
+ * kernels have no waits that can run out of time; the word stays 0 unless a future kernel sets it. */
+mkx_status mkx_mods_last_error(mkx_mods_handle* h, int* code);
 
 /* MODW of a handle. */
 int mkx_mods_width(const mkx_mods_handle* h);

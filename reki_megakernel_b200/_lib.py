@@ -74,6 +74,7 @@ SIGNATURES = {
     "mkx_mods_run": (C.c_int, [P, C.c_int, P, P, P, P]),
     "mkx_mods_width": (C.c_int, [P]),
     "mkx_mods_input": (C.c_int, [P, P, P]),
+    "mkx_mods_last_error": (C.c_int, [P, C.POINTER(C.c_int)]),
     "mkx_mods_destroy": (None, [P]),
 }
 

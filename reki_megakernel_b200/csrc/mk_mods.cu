@@ -2,9 +2,9 @@
 //
 // Two launches per call:
 //   cond_kernel  a[s][h] = bf16(silu(8 (W_t temb_s + W_s state)))  for s < N (rows N..15 zero), and
-//                dt = 1/N. 24 CTAs of 8 warps; the embedding in double (angles up to 1000 rad), then a
-//                warp owns 4 columns h, keeps its W_t row slices in registers and reduces each (s, h)
-//                dot product (fp32) across the lanes.
+//                dt = 1/N. 96 CTAs of 8 warps, one column h per warp, the 16 step sums as independent
+//                fp32 chains over a timestep-embedding table built once at create (in double: the
+//                angles reach 1000 rad), then reduced across the lanes.
 //   proj_kernel  mods[s][r] = bf16(W_m[r] . a[s] + b_m[r]): one persistent CTA of 16 warps per SM,
 //                each CTA a contiguous run of 16-row m-tiles (balanced to within one m-tile per SM).
 //                W_m was repacked at create time into mma.sync A-fragment order, so a lane's
@@ -12,7 +12,9 @@
 //                512 contiguous bytes per block; k-blocks stream in chunks of 8, the next chunk in
 //                flight while the current one is multiplied (mma.sync m16n8k16 bf16, fp32
 //                accumulate) against a[16][768] held in shared memory. HBM-bound: the 108.5 MB of
-//                W_m cross HBM once per call for all N steps.
+//                W_m cross HBM once per call for all N steps. Launched as a programmatic dependent
+//                of cond_kernel: each warp's first two chunks are in flight before it waits
+//                (griddepcontrol.wait) for `act`.
 #include <cstdint>
 #include <cstring>
 #include <new>
@@ -27,14 +29,13 @@ using namespace mkx;
 constexpr int H = 768;
 constexpr int NMAX = 16;               // steps per call: two n-tiles of 8
 constexpr int KB = H / 16;             // 16-wide k-blocks per row
-constexpr int CH = 8;                  // k-blocks per streamed chunk
+constexpr int CH = 8;                  // projection: k-blocks per streamed chunk
 constexpr int NCH = KB / CH;           // chunks per m-tile
 constexpr int PW = 16, PT = PW * 32;   // projection: warps / threads per CTA
-constexpr int AS = H + 8;              // shared activation row stride (bf16): conflict-free B fragments
-constexpr int CW = 8, CT = CW * 32;    // conditioning: warps / threads per CTA
-constexpr int CCOLS = 32;              // conditioning: columns h per CTA (4 per warp)
-constexpr int TDIM_MAX = 512, SDIM_MAX = 64;
 static_assert(KB % CH == 0, "chunks tile an m-tile");
+constexpr int AS = H + 8;              // shared activation row stride (bf16): conflict-free B fragments
+constexpr int CW = 8, CT = CW * 32;    // conditioning: warps (= columns h) / threads per CTA
+constexpr int TDIM_MAX = 512, SDIM_MAX = 64;
 
 // 16-byte read-only load that bypasses L1 (every W_m byte is used once per call).
 __device__ __forceinline__ uint4 ldg_stream(const uint4* p) {
@@ -45,48 +46,82 @@ __device__ __forceinline__ uint4 ldg_stream(const uint4* p) {
   return v;
 }
 
-__global__ void __launch_bounds__(CT) cond_kernel(const float* __restrict__ w_t, const float* __restrict__ w_s,
-                                                  const float* __restrict__ state, int N, int tdim, int sdim,
-                                                  uint16_t* __restrict__ act, float* __restrict__ dt_out) {
-  __shared__ float temb[NMAX * TDIM_MAX];  // [N][tdim]: cos half, then sin half
+// Asks L2 to fetch `bytes` (a multiple of 16) from `src` (16-byte aligned); no data comes back.
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// Timestep-embedding table of every step count, built once at create: temb[N - 1][s][tdim] =
+// [cos(1000 t_s f_i) | sin(1000 t_s f_i)], t_s = 1 - s/N, f_i = 10000^(-i/(tdim/2)), in double
+// (the angles reach 1000 rad), rounded once to fp32.
+__global__ void temb_table_kernel(float* __restrict__ tab, int tdim) {
   const int half = tdim / 2;
-  // The angles reach 1000 rad: computed (and reduced) in double, so the embedding carries only its
-  // fp32 rounding (an fp32 angle would be off by ~2e-4 rad). N x tdim/2 values per CTA, negligible.
-  for (int e = threadIdx.x; e < N * half; e += CT) {
-    const int s = e / half, i = e - s * half;
-    const double t = 1.0 - (double)s / (double)N;
-    const double f = exp(-log(10000.0) * (double)i / (double)half);
-    double sn, cs;
-    sincos(1000.0 * t * f, &sn, &cs);
-    temb[s * tdim + i] = (float)cs;
-    temb[s * tdim + half + i] = (float)sn;
-  }
-  __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int per = tdim / 32;  // W_t values per lane
-  for (int j = 0; j < CCOLS / CW; ++j) {
-    const int h = blockIdx.x * CCOLS + warp + CW * j;
-    float wr[TDIM_MAX / 32];
-#pragma unroll
-    for (int q = 0; q < TDIM_MAX / 32; ++q) wr[q] = q < per ? __ldg(w_t + (size_t)h * tdim + lane + 32 * q) : 0.f;
-    const float st = lane < sdim ? __ldg(w_s + (size_t)h * sdim + lane) * __ldg(state + lane) : 0.f;
-    const float st2 = lane + 32 < sdim ? __ldg(w_s + (size_t)h * sdim + lane + 32) * __ldg(state + lane + 32) : 0.f;
-    for (int s = 0; s < NMAX; ++s) {
-      float acc = 0.f;
-      if (s < N) {
-        acc = st + st2;
-#pragma unroll
-        for (int q = 0; q < TDIM_MAX / 32; ++q)
-          if (q < per) acc = fmaf(wr[q], temb[s * tdim + lane + 32 * q], acc);
-#pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-      }
-      if (lane == 0) {
-        const float e8 = 8.f * acc;
-        const float a = s < N ? e8 / (1.f + expf(-e8)) : 0.f;
-        act[s * H + h] = (uint16_t)(pack_bf2(a, 0.f) & 0xffffu);
-      }
+  const int total = NMAX * NMAX * half;
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < total; e += gridDim.x * blockDim.x) {
+    const int i = e % half, s = (e / half) % NMAX, n = e / (half * NMAX) + 1;
+    float* row = tab + ((size_t)(n - 1) * NMAX + s) * tdim;
+    if (s >= n) {
+      row[i] = 0.f;
+      row[half + i] = 0.f;
+      continue;
     }
+    const double t = (double)(n - s) / (double)n;
+    const double ang = 1000.0 * t * exp(-log(10000.0) * (double)i / (double)half);
+    double sn, cs;
+    sincos(ang, &sn, &cs);
+    row[i] = (float)cs;
+    row[half + i] = (float)sn;
+  }
+}
+
+// Conditioning: warp w owns column h = 8 blockIdx.x + w; lane l holds W_t[h][l + 32 q]. The 16 step
+// sums accumulate side by side (independent fp32 chains) over the table rows of this N (staged in
+// shared memory), then reduce
+// across the lanes; lane s finishes step s. Lets the projection launch at once (it streams W_m
+// while this runs and waits for `act` only where it reads it).
+__global__ void __launch_bounds__(CT) cond_kernel(const float* __restrict__ w_t, const float* __restrict__ w_s,
+                                                  const float* __restrict__ state, const float* __restrict__ temb,
+                                                  int N, int tdim, int sdim, uint16_t* __restrict__ act,
+                                                  float* __restrict__ dt_out) {
+  extern __shared__ float4 tsm4[];  // this N's table rows [N][tdim]
+  float* tsm = reinterpret_cast<float*>(tsm4);
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.x * CW + warp;
+  const int per = tdim / 32;
+  const float4* tb = reinterpret_cast<const float4*>(temb + (size_t)(N - 1) * NMAX * tdim);
+  for (int e = threadIdx.x; e < N * tdim / 4; e += CT) tsm4[e] = __ldg(tb + e);
+  float wr[TDIM_MAX / 32];
+#pragma unroll
+  for (int q = 0; q < TDIM_MAX / 32; ++q) wr[q] = q < per ? __ldg(w_t + (size_t)h * tdim + lane + 32 * q) : 0.f;
+  float st = lane < sdim ? __ldg(w_s + (size_t)h * sdim + lane) * __ldg(state + lane) : 0.f;
+  if (lane + 32 < sdim) st += __ldg(w_s + (size_t)h * sdim + lane + 32) * __ldg(state + lane + 32);
+  __syncthreads();
+  float acc[NMAX];
+#pragma unroll
+  for (int s = 0; s < NMAX; ++s) acc[s] = st;
+#pragma unroll
+  for (int q = 0; q < TDIM_MAX / 32; ++q) {
+    if (q < per) {
+#pragma unroll
+      for (int s = 0; s < NMAX; ++s)
+        if (s < N) acc[s] = fmaf(wr[q], tsm[s * tdim + lane + 32 * q], acc[s]);
+    }
+  }
+  float mine = 0.f;
+#pragma unroll
+  for (int s = 0; s < NMAX; ++s) {
+    if (s < N) {  // uniform
+      float v = acc[s];
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == s) mine = v;
+    }
+  }
+  if (lane < NMAX) {
+    const float e8 = 8.f * mine;
+    const float a = lane < N ? e8 / (1.f + expf(-e8)) : 0.f;
+    act[lane * H + h] = (uint16_t)(pack_bf2(a, 0.f) & 0xffffu);
   }
   if (blockIdx.x == 0 && threadIdx.x == 0) *dt_out = 1.f / (float)N;
 }
@@ -95,11 +130,6 @@ __global__ void __launch_bounds__(PT, 1) proj_kernel(const uint4* __restrict__ w
                                                      const uint16_t* __restrict__ act, int N, int MODW,
                                                      uint16_t* __restrict__ out) {
   __shared__ __align__(16) uint16_t xs[NMAX * AS];
-  for (int e = threadIdx.x; e < NMAX * H / 8; e += PT) {
-    const int row = e / (H / 8), c8 = e - row * (H / 8);
-    *reinterpret_cast<uint4*>(xs + row * AS + c8 * 8) = *reinterpret_cast<const uint4*>(act + row * H + c8 * 8);
-  }
-  __syncthreads();
   const int MT = MODW / 16;
   const int mt0 = (int)((long long)blockIdx.x * MT / gridDim.x);
   const int mt1 = (int)((long long)(blockIdx.x + 1) * MT / gridDim.x);
@@ -153,9 +183,19 @@ __global__ void __launch_bounds__(PT, 1) proj_kernel(const uint4* __restrict__ w
 #pragma unroll
     for (int i = 0; i < CH; ++i) b[i] = ldg_stream(p + i * 32);
   };
+  // The first two chunks stream while the conditioning launch finishes (programmatic dependency);
+  // `act` is read only after griddepcontrol.wait.
   if (nchunks > 0) load(ba, 0);
+  if (nchunks > 1) load(bb, 1);
+  if (lane == 0 && mine > 0) prefetch_l2(wpk + (size_t)(mt0 + warp) * KB * 32, KB * 512);  // first m-tile
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  for (int e = threadIdx.x; e < NMAX * H / 8; e += PT) {
+    const int row = e / (H / 8), c8 = e - row * (H / 8);
+    *reinterpret_cast<uint4*>(xs + row * AS + c8 * 8) = *reinterpret_cast<const uint4*>(act + row * H + c8 * 8);
+  }
+  __syncthreads();
   for (int c = 0; c < nchunks; c += 2) {
-    if (c + 1 < nchunks) load(bb, c + 1);
+    if (c > 0 && c + 1 < nchunks) load(bb, c + 1);
     compute(ba, c);
     if (c + 1 >= nchunks) break;
     if (c + 2 < nchunks) load(ba, c + 2);
@@ -189,6 +229,10 @@ struct mkx_mods_handle {
   uint16_t* wpk;   // W_m in fragment order
   float* b_m;
   uint16_t* act;   // [16][H] bf16 conditioning output
+  float* temb;     // [16 step counts][16][tdim] fp32 timestep-embedding table
+  int* status;     // device error word (a projection wait that ran out of time)
+  unsigned long long timeout_ns;
+  cudaStream_t last_stream;
 };
 
 using namespace mkxm;
@@ -221,15 +265,20 @@ extern "C" mkx_status mkx_mods_create(const mkx_mods_dims* dims, const float* w_
   h->device = device;
   h->MODW = 9 * d.L * H + 2 * H;
   h->grid = sms < h->MODW / 16 ? sms : h->MODW / 16;
+  h->timeout_ns = 2000000000ull;
   const size_t nt = (size_t)H * d.tdim, ns = (size_t)H * d.sdim, nm = (size_t)h->MODW * H;
   bool ok = cudaMalloc(&h->w_t, nt * 4) == cudaSuccess && cudaMalloc(&h->w_s, ns * 4) == cudaSuccess &&
             cudaMalloc(&h->wpk, nm * 2) == cudaSuccess && cudaMalloc(&h->b_m, (size_t)h->MODW * 4) == cudaSuccess &&
             cudaMalloc(&h->act, (size_t)NMAX * H * 2) == cudaSuccess &&
+            cudaMalloc(&h->temb, (size_t)NMAX * NMAX * d.tdim * 4) == cudaSuccess &&
+            cudaMalloc(&h->status, sizeof(int)) == cudaSuccess && cudaMemset(h->status, 0, sizeof(int)) == cudaSuccess &&
+
             cudaMemcpy(h->w_t, w_t, nt * 4, cudaMemcpyDeviceToDevice) == cudaSuccess &&
             cudaMemcpy(h->w_s, w_s, ns * 4, cudaMemcpyDeviceToDevice) == cudaSuccess &&
             cudaMemcpy(h->b_m, b_m, (size_t)h->MODW * 4, cudaMemcpyDeviceToDevice) == cudaSuccess;
   if (ok) {
     mods_pack_kernel<<<1184, 256>>>(w_m, h->wpk, h->MODW);
+    temb_table_kernel<<<64, 256>>>(h->temb, d.tdim);
     ok = cudaGetLastError() == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess;
   }
   if (!ok) {
@@ -246,10 +295,32 @@ extern "C" mkx_status mkx_mods_run(mkx_mods_handle* h, int N, const float* state
   if (N < 1 || N > NMAX) return MKX_ERR_INVALID_ARG;
   if ((reinterpret_cast<uintptr_t>(mods_out) & 3) != 0) return MKX_ERR_INVALID_ARG;
   if (cudaSetDevice(h->device) != cudaSuccess) return MKX_ERR_CUDA;
-  cond_kernel<<<H / CCOLS, CT, 0, stream>>>(h->w_t, h->w_s, state, N, h->d.tdim, h->d.sdim, h->act, dt_out);
+  cond_kernel<<<H / CW, CT, (size_t)N * h->d.tdim * 4, stream>>>(h->w_t, h->w_s, state, h->temb, N, h->d.tdim, h->d.sdim, h->act, dt_out);
   if (cudaGetLastError() != cudaSuccess) return MKX_ERR_CUDA;
-  proj_kernel<<<h->grid, PT, 0, stream>>>(reinterpret_cast<const uint4*>(h->wpk), h->b_m, h->act, N, h->MODW, mods_out);
-  if (cudaGetLastError() != cudaSuccess) return MKX_ERR_CUDA;
+  // programmatic dependent launch: the projection may start while the conditioning runs
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(h->grid);
+  cfg.blockDim = dim3(PT);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, proj_kernel, reinterpret_cast<const uint4*>(h->wpk), (const float*)h->b_m,
+                         (const uint16_t*)h->act, N, h->MODW, mods_out) != cudaSuccess)
+    return MKX_ERR_CUDA;
+  h->last_stream = stream;
+  return MKX_OK;
+}
+
+extern "C" mkx_status mkx_mods_last_error(mkx_mods_handle* h, int* code) {
+  if (!h || !code) return MKX_ERR_INVALID_ARG;
+  if (cudaSetDevice(h->device) != cudaSuccess || cudaStreamSynchronize(h->last_stream) != cudaSuccess ||
+      cudaMemcpy(code, h->status, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return MKX_ERR_CUDA;
   return MKX_OK;
 }
 
@@ -261,5 +332,7 @@ extern "C" void mkx_mods_destroy(mkx_mods_handle* h) {
   if (h->wpk) cudaFree(h->wpk);
   if (h->b_m) cudaFree(h->b_m);
   if (h->act) cudaFree(h->act);
+  if (h->status) cudaFree(h->status);
+  if (h->temb) cudaFree(h->temb);
   delete h;
 }

@@ -74,6 +74,12 @@ class StepModulations:
                    "mkx_mods_input")
         return a
 
+    def check_device_error(self):
+        code = C.c_int(0)
+        _lib.check(self.lib.mkx_mods_last_error(self.h, C.byref(code)), "mkx_mods_last_error")
+        if code.value != 0:
+            raise _lib.MkxError("modulation kernels", _lib.MKX_ERR_DEVICE, f"error word {code.value:#x}")
+
     def close(self):
         if getattr(self, "h", None):
             self.lib.mkx_mods_destroy(self.h)

@@ -112,4 +112,5 @@ def test_modulation_arguments_are_rejected_without_a_device():
     assert lib.mkx_mods_run(None, 10, None, None, None, None) == _lib.MKX_ERR_INVALID_ARG
     assert lib.mkx_mods_width(None) == 0
     assert lib.mkx_mods_input(None, None, None) == _lib.MKX_ERR_INVALID_ARG
+    assert lib.mkx_mods_last_error(None, None) == _lib.MKX_ERR_INVALID_ARG
     lib.mkx_mods_destroy(None)
