@@ -214,7 +214,7 @@ __device__ __forceinline__ void issue_slot(const Params& p, Cta& c, int slot, in
   const uint32_t bytes = slot_bytes(p, c, slot);
   fence_proxy_async();
   mbar_expect_tx(&cBar(p, c)[slot], bytes);
-  bulk_g2s(cSlot(p, c, slot), slot_src(p, c, slot, l), bytes, &cBar(p, c)[slot]);
+  bulk_g2s_hint(cSlot(p, c, slot), slot_src(p, c, slot, l), bytes, &cBar(p, c)[slot], l2_evict_first());
   cCnt(p, c)[slot] += 1;
 }
 
@@ -234,8 +234,8 @@ __device__ __forceinline__ void issue_mods(const Params& p, Cta& c, int q) {
   const int b = BAR_MODS + (q & 1);
   fence_proxy_async();
   mbar_expect_tx(&cBar(p, c)[b], bytes);
-  bulk_g2s(cMods(p, c) + (size_t)(q & 1) * 3 * H * sizeof(ModT), reinterpret_cast<const ModT*>(p.mods) + off, bytes,
-           &cBar(p, c)[b]);
+  bulk_g2s_hint(cMods(p, c) + (size_t)(q & 1) * 3 * H * sizeof(ModT), reinterpret_cast<const ModT*>(p.mods) + off, bytes,
+           &cBar(p, c)[b], l2_evict_first());
   cCnt(p, c)[b] += 1;
 }
 template <typename ModT>
@@ -672,6 +672,7 @@ __device__ __forceinline__ int attention_unit(const Params& p, Cta& c, const boo
   // Load chunk 0 of K/V and the per-row tables; none of it depends on the exchange, and the pinned
   // loads are in flight while the query is polled.
   uint2 kA[MAXK], kB[MAXK], vA[MAXK], vB[MAXK];
+  const uint64_t keep = l2_evict_last();  // K/V are re-read every Euler step: keep them in L2
   auto load_chunk = [&](int base) {
 #pragma unroll
     for (int i = 0; i < MAXK; ++i) {
@@ -680,10 +681,10 @@ __device__ __forceinline__ int attention_unit(const Params& p, Cta& c, const boo
       if (j < nkeys) {
         const uint16_t* kr = Kb + (size_t)j * stride + h * HD + d0;
         const uint16_t* vr = Vb + (size_t)j * stride + h * HD + d0;
-        kA[i] = ldg_u2_pin(kr);
-        kB[i] = ldg_u2_pin(kr + 8);
-        vA[i] = ldg_u2_pin(vr);
-        vB[i] = ldg_u2_pin(vr + 8);
+        kA[i] = ldg_u2_pin_hint(kr, keep);
+        kB[i] = ldg_u2_pin_hint(kr + 8, keep);
+        vA[i] = ldg_u2_pin_hint(vr, keep);
+        vB[i] = ldg_u2_pin_hint(vr + 8, keep);
       }
     }
   };
