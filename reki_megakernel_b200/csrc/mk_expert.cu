@@ -726,8 +726,6 @@ __device__ __forceinline__ int attention_unit(const Params& p, Cta& c, const boo
     bf_words_to_lane(ko, payload_of(w0[2]), payload_of(w1[2]), payload_of(w0[3]), payload_of(w1[3]));
     bf_words_to_lane(vo, payload_of(w0[4]), payload_of(w1[4]), payload_of(w0[5]), payload_of(w1[5]));
     norm_rope(ko, wk, ck, sk, p.qk_eps, l8);  // all lanes: the shuffles need the full warp
-    const float so = dot8(q, ko) * p.sm_scale;
-    if (own) s_own = so;
   }
 
   float m_run = -INFINITY, den = 0.f;
@@ -736,21 +734,34 @@ __device__ __forceinline__ int attention_unit(const Params& p, Cta& c, const boo
   bool checked = false;  // the poll's failure flag went through a block_max barrier
   for (int base = kbeg; base < nkeys || (SA && base == kbeg); base += NG * MAXK, ++chunk) {
     if (base != kbeg) load_chunk(base);
-    float s[MAXK];
-    float mloc = (SA && base == kbeg) ? s_own : -INFINITY;
+    // Scores of the MAXK key slots (and, on SA's first chunk, of the own row): every slot's 8-term
+    // lane sum first, then each group-of-8 shuffle level across all slots at once (the same
+    // reduction order as dot8, without a shuffle chain per slot). Slots without a key hold zero K
+    // and are masked below; all lanes run every shuffle.
+    const bool with_own = SA && base == kbeg;  // uniform
+    float s[MAXK + 1];
+#pragma unroll
+    for (int i = 0; i <= MAXK; ++i) {
+      s[i] = 0.f;
+      if (i < MAXK || with_own) {
+        Lane8 k;
+        if (i < MAXK) bf_nat_to_lane(k, kA[i], kB[i]);
+        else k = ko;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) s[i] = fmaf(q.v[e], k.v[e], s[i]);
+      }
+    }
+#pragma unroll
+    for (int lv = 1; lv <= 4; lv <<= 1)
+#pragma unroll
+      for (int i = 0; i <= MAXK; ++i)
+        if (i < MAXK || with_own) s[i] += __shfl_xor_sync(0xffffffffu, s[i], lv);
+    if (with_own && own) s_own = s[MAXK] * p.sm_scale;
+    float mloc = with_own ? s_own : -INFINITY;
 #pragma unroll
     for (int i = 0; i < MAXK; ++i) {
-      // Key slot i holds a valid key for some groups only when nkeys - base is not a multiple of
-      // NG: the group-of-8 shuffles in dot8 must still run on every lane of the warp.
-      if (base + NG * i >= nkeys) {  // uniform: no group has a key in this slot
-        s[i] = -INFINITY;
-        continue;
-      }
       const int j = base + kg + NG * i;
-      Lane8 k;
-      bf_nat_to_lane(k, kA[i], kB[i]);
-      const float dv = dot8(q, k) * p.sm_scale;
-      s[i] = j < nkeys ? dv : -INFINITY;
+      s[i] = j < nkeys ? s[i] * p.sm_scale : -INFINITY;
       mloc = fmaxf(mloc, s[i]);
     }
     int any_fail;
