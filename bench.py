@@ -227,6 +227,68 @@ def run_timeline(args):
     print(json.dumps(out), flush=True)
 
 
+def run_predict(args):
+    """The GPU half of one predict after Euler step 1 (BASELINE configs[2] without step 1 and the VLM):
+    modulation rows, cross-attention K/V of all layers and Euler steps 2..N replayed as one CUDA graph
+    (PredictGraph). Prints one JSON line (not the headline metric)."""
+    from reki_megakernel_b200.mk_expert import ExpertMegakernel
+    from reki_megakernel_b200.modulations import StepModulations
+    from reki_megakernel_b200.predict import PredictGraph
+    from reki_megakernel_b200.prepare import RegisterPrepare
+    from reki_megakernel_b200.synthetic import (ExpertDims, make_inputs, make_modulation_weights, make_prepare_weights,
+                                                make_source, make_state, make_weights)
+    dims = ExpertDims()
+    S = args.S
+    mk = ExpertMegakernel(weights=make_weights(dims, seed=0).to("cuda"))
+    rp = RegisterPrepare(make_prepare_weights(dims, seed=0).to("cuda"))
+    sm = StepModulations(make_modulation_weights(dims, seed=0).to("cuda"))
+    inp = make_inputs(dims, S=S).to("cuda")
+    pg = PredictGraph(mk, rp, sm, num_steps=10, S=S, T=10, memk=inp.memk[0], memv=inp.memv[0],
+                      kv_start=int(inp.kv_start[0]), action_dim=inp.action_dim)
+    src = make_source(S, dims.src_dim, seed=0).to("cuda")
+    state = make_state(sm.sdim, seed=0).to("cuda")
+    x_t = inp.x[:1].contiguous()
+    pg(src, state, x_t)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    for _ in range(args.warmup):
+        pg.graph.replay()
+    torch.cuda.synchronize()
+    pg.check_device_errors()
+    clocks = Clocks(0)
+    clocks.start()
+    time.sleep(0.3)
+    per = []
+    for _ in range(args.steps):
+        flush.fill_(1)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        pg.graph.replay()
+        b.record()
+        b.synchronize()
+        per.append(a.elapsed_time(b))
+    clk = clocks.stop()
+    pg.check_device_errors()
+    ms = statistics.mean(per)
+    L, H = dims.L, dims.H
+    wbytes = (9 * algorithmic_bytes_per_step(dims, dims.MODW * 2) + dims.MODW * H * 2 + dims.MODW * 4
+              + L * 2 * H * dims.src_dim * 2)
+    hbm, peak_kind = peaks()
+    achieved = wbytes / (ms * 1e-3) / 1e9
+    line = {
+        "metric": "GPU half of a predict after step 1: modulations + register_prepare + Euler steps 2-10, ms",
+        "value": ms, "unit": "ms", "higher_is_better": False, "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "dtype": "bf16", "data": "synthetic (seeded weights and inputs)",
+        "config": {"workload": f"one CUDA graph: 10 modulation rows, K/V of {L} layers from S={S} source rows, "
+                               "9 Euler steps of the expert", "S": S, "T": 10, "euler_steps": 9,
+                   "l2": "256 MB written between timed replays (untimed)"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_kind": f"{peak_kind} (hbm copy, burst)", "algorithmic_bytes": wbytes},
+        "gpu_launches": 4 * args.steps,
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_mods(args):
     """Per-step modulation rows of one predict (BASELINE configs[2]'s modulation part): N = 10 rows of
     MODW = 70,656 from the conditioning network, two launches (conditioning + HBM-bound projection).
@@ -560,14 +622,17 @@ def main():
     ap.add_argument("--timeline", action="store_true", help="per-stage critical path of one predict, no bench line")
     ap.add_argument("--prepare", action="store_true", help="time register_prepare (cross-attention K/V), own JSON line")
     ap.add_argument("--mods", action="store_true", help="time the per-step modulation rows (_step_modulations), own JSON line")
+    ap.add_argument("--predict", action="store_true",
+                    help="time the GPU half of a predict after step 1 (modulations + K/V preparation + expert) as one graph")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    if args.timeline or args.prepare or args.mods:
+    if args.timeline or args.prepare or args.mods or args.predict:
         if rank == 0:
-            (run_timeline if args.timeline else run_prepare if args.prepare else run_mods)(args)
+            (run_timeline if args.timeline else run_prepare if args.prepare else run_mods if args.mods
+             else run_predict)(args)
         return
     if world > 1:
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
