@@ -101,6 +101,16 @@ typedef struct {
   uint16_t* trace_h;      /* optional [n_steps, L, T, H] bf16: every layer's output h; may be NULL */
   unsigned long long* prof; /* optional [grid, 1 + mkx_sync_points(n_steps)] %globaltimer stamps (ns):
                              * per CTA, the launch start then the end of every stage; may be NULL */
+  /* optional (no counterpart in the reference, whose K/V are always on the device): readiness words
+   * for K/V that are still being copied in while the launch runs. When kv_ready is non-NULL
+   * (device int32 [L], 4-byte aligned), the launch reads layer l's memory and cross-attention K/V
+   * only once kv_ready[l] == kv_ready_value; the caller writes that value after the layer's copies,
+   * in the same copy stream (a 4-byte host-to-device copy: a kernel there would wait for the SMs
+   * this launch holds). A word that never arrives ends the launch with a timeout error
+   * (mkx_last_error) instead of a hang. NULL: every input is in place at launch. Read by mkx_run;
+ * mkx_run_static ignores these two fields. */
+  const int* kv_ready;
+  int kv_ready_value;
 } mkx_step_inputs;
 
 /* Packs the weights into the handle's own device memory (one-off, synchronous on `stream`'s
@@ -164,6 +174,12 @@ typedef struct {
  * whose launches overlap on the GPU race and corrupt each other. */
 mkx_status mkx_run_static(const mkx_dims* dims, const mkx_packed_weights* w, const mkx_step_inputs* in,
                           int* err_out, cudaStream_t stream);
+
+/* Enqueues n host-to-device copies on `stream`, one cudaMemcpyAsync each, in order: dst[i] (device)
+ * <- src[i] (pinned host), bytes[i] bytes. The copies of a streamed launch (the small inputs ahead of
+ * it, then per layer its K/V followed by its 4-byte readiness word, see kv_ready) are issued with
+ * one call each instead of one host call per tensor. No counterpart in the reference. */
+mkx_status mkx_h2d_copies(int n, void* const* dst, const void* const* src, const size_t* bytes, cudaStream_t stream);
 
 /* Last CUDA error string seen by the library (thread-local, static storage). */
 const char* mkx_last_cuda_error(void);

@@ -38,7 +38,8 @@ class StepInputs(C.Structure):
                 ("kca", P * MAX_LAYERS), ("vca", P * MAX_LAYERS), ("ca_rows", C.c_int), ("ca_row_stride", C.c_int),
                 ("cu_src", P),
                 ("sa_cos", P), ("sa_sin", P), ("ca_cos", P), ("ca_sin", P),
-                ("T", C.c_int), ("n_steps", C.c_int), ("action_dim", C.c_int), ("trace_h", P), ("prof", P)]
+                ("T", C.c_int), ("n_steps", C.c_int), ("action_dim", C.c_int), ("trace_h", P), ("prof", P),
+                ("kv_ready", P), ("kv_ready_value", C.c_int)]
 
 
 class PackedWeights(C.Structure):
@@ -65,6 +66,7 @@ SIGNATURES = {
     "mkx_launch_shape": (C.c_int, [P, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
     "mkx_run_static": (C.c_int, [C.POINTER(Dims), C.POINTER(PackedWeights), C.POINTER(StepInputs), P, P]),
     "mkx_last_cuda_error": (C.c_char_p, []),
+    "mkx_h2d_copies": (C.c_int, [C.c_int, P, P, P, P]),
     "mkx_destroy": (None, [P]),
     "mkx_prep_create": (C.c_int, [C.POINTER(PrepDims), P, P, C.c_int, C.POINTER(P)]),
     "mkx_prep_run": (C.c_int, [P, P, C.c_int, P, P, P, P, C.c_int, P]),

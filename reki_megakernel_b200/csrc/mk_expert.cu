@@ -99,6 +99,8 @@ struct Params {
   const float* ca_sin;
   uint16_t* trace_h;
   unsigned long long* prof;
+  const int* kv_ready;            // optional per-layer readiness words of streamed-in K/V
+  int kv_ready_value;
   unsigned long long timeout_ns;
   int drop_stage;                 // test hook: CTA 0 withholds its layer-0 words of this stage
   int mem_rows, mem_row_stride, ca_rows, ca_row_stride;
@@ -1195,7 +1197,22 @@ __device__ __forceinline__ int stage_down(const Params& p, Cta& c, int gi, int q
 }
 
 // Self-attention (sa) or cross-attention, one (head, row) unit per CTA; one routine for both.
+// Streamed inputs: before the first Euler step's self-attention of layer l reads any K/V, thread 0
+// waits (bounded) until kv_ready[l] holds this launch's value. The copies of layer l's memory and
+// cross-attention K/V precede that word in their stream, so both attention stages of the layer see
+// them; later Euler steps find them in place.
+__device__ __forceinline__ int wait_kv_ready(const Params& p, Cta& c, int l) {
+  int r = 0;
+  if (c.tid == 0) {
+    Waiter wt(p.status, p.timeout_ns);
+    while (r == 0 && ld_acquire_i32(p.kv_ready + l) != p.kv_ready_value) r = wt.tick();
+    r = fail_code(p, c, r, ST_SA);
+  }
+  return __syncthreads_or(r);
+}
+
 __device__ __forceinline__ int stage_attention(const Params& p, Cta& c, const bool sa, int gi, int l) {
+  if (sa && p.kv_ready != nullptr && gi < p.L && c.cta < NH * p.T && wait_kv_ready(p, c, l)) return 1;
   const int par = gi & 1;
   const uint32_t tag = c.tag0 + (uint32_t)gi;
   const u64* src = sa ? p.xb[B_QKV] + (size_t)par * TP * QKVWORDS : p.xb[B_QCA] + (size_t)par * TP * HWORDS;
@@ -1445,6 +1462,16 @@ static mkx_status cuda_fail(cudaError_t e, const char* what) {
 
 extern "C" const char* mkx_last_cuda_error(void) { return g_cuda_err; }
 
+extern "C" mkx_status mkx_h2d_copies(int n, void* const* dst, const void* const* src, const size_t* bytes,
+                                     cudaStream_t stream) {
+  if (n < 0 || (n > 0 && (!dst || !src || !bytes))) return MKX_ERR_INVALID_ARG;
+  for (int i = 0; i < n; ++i) {
+    if (!dst[i] || !src[i]) return MKX_ERR_INVALID_ARG;
+    MKX_CUDA(cudaMemcpyAsync(dst[i], src[i], bytes[i], cudaMemcpyHostToDevice, stream));
+  }
+  return MKX_OK;
+}
+
 static bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 
 static void* halloc(mkx_handle* h, size_t bytes, cudaError_t* err) {
@@ -1643,6 +1670,7 @@ extern "C" mkx_status mkx_run(mkx_handle* h, const mkx_step_inputs* in, cudaStre
   if (!in->x_in || !in->x_out || !in->mods || !in->dt || !in->cu_kv || !in->cu_src || !in->sa_cos || !in->sa_sin ||
       !in->ca_cos || !in->ca_sin)
     return MKX_ERR_INVALID_ARG;
+  if (in->kv_ready && (reinterpret_cast<uintptr_t>(in->kv_ready) & 3u)) return MKX_ERR_INVALID_ARG;
   if (in->mem_rows < 1 || in->mem_rows > MAX_MEM_ROWS || in->ca_rows < 1) return MKX_ERR_UNSUPPORTED;
   if (in->mem_row_stride < H || in->mem_row_stride % 8 || in->ca_row_stride < H || in->ca_row_stride % 8)
     return MKX_ERR_INVALID_ARG;
@@ -1677,6 +1705,8 @@ extern "C" mkx_status mkx_run(mkx_handle* h, const mkx_step_inputs* in, cudaStre
   p.ca_sin = in->ca_sin;
   p.trace_h = in->trace_h;
   p.prof = in->prof;
+  p.kv_ready = in->kv_ready;
+  p.kv_ready_value = in->kv_ready_value;
   p.timeout_ns = h->timeout_ns;
   p.drop_stage = h->drop_stage;
   p.T = in->T;

@@ -11,6 +11,11 @@ Same names, arguments and behaviour as the reference launcher:
   ``past.cross_attn_kv`` in place: the per-layer K/V tensors are passed by pointer, no stacking copy.
   No host synchronisation happens, so the call can be captured in a CUDA graph (the reference's
   launch sits inside Kyutai's expert graph).
+* ``.run_from_host(x_t, mods, dt, past, action_dim)``: the same launch for callers whose inputs sit
+  in pinned host memory (no counterpart in the reference). The small inputs are copied ahead of the
+  launch; each layer's memory and cross-attention K/V are copied on a side stream while the launch
+  already runs, and the kernel waits (bounded) for a per-layer readiness word before its first read
+  of them, so the copies overlap the first Euler step instead of preceding the launch.
 * ``.barriers(n_steps)`` keeps the reference's count ``1 + n_steps (8 L + 1)``
   (``src/mk_expert.py:517-518``): the number of dependent exchange points of one launch.
 * ``install(model)`` rebinds ``model._expert_actions`` exactly like ``src/mk_expert.py:521-536``.
@@ -22,6 +27,7 @@ There is no CPU path: without ``libmkx.so`` the import fails.
 from __future__ import annotations
 
 import ctypes as C
+from types import SimpleNamespace
 
 import torch
 
@@ -85,9 +91,23 @@ class ExpertMegakernel:
         return self._dt_cache[key]
 
     def run(self, x_t: torch.Tensor, mods: torch.Tensor, dt, past, action_dim: int,
-            trace: torch.Tensor | None = None, prof: torch.Tensor | None = None) -> torch.Tensor:
+            trace: torch.Tensor | None = None, prof: torch.Tensor | None = None,
+            kv_ready: torch.Tensor | None = None, kv_ready_value: int = 0) -> torch.Tensor:
         """x_t: [1, T, A] fp32 after Euler step 1; mods: [N, MODW] (row 0 = step 1, used already);
-        returns x_t after step N (padded dims as the reference: 0 + dt * v)."""
+        returns x_t after step N (padded dims as the reference: 0 + dt * v). kv_ready (optional,
+        int32 [L] on the device): the launch reads layer l's K/V only once kv_ready[l] equals
+        kv_ready_value (see ``run_from_host``)."""
+        si, out, keep = self._step_inputs(x_t, mods, dt, past, action_dim, trace, prof, kv_ready, kv_ready_value)
+        self._launch(si)
+        return out
+
+    def _launch(self, si) -> None:
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        _lib.check(self._lib.mkx_run(self._h, C.byref(si), C.c_void_p(stream)), "mkx_run")
+
+    def _step_inputs(self, x_t, mods, dt, past, action_dim, trace, prof, kv_ready, kv_ready_value):
+        """Validated launch descriptor, the fresh output tensor, and the tensors the descriptor points
+        to that were made here (kept alive by the caller until the launch is enqueued)."""
         step = past.register_step
         if x_t.dim() != 3 or x_t.shape[0] != 1 or x_t.shape[2] != self.A:
             raise ValueError(f"x_t must be [1, T, {self.A}], got {tuple(x_t.shape)}")
@@ -157,15 +177,118 @@ class ExpertMegakernel:
         si.cu_kv, si.cu_src = cu_kv.data_ptr(), cu_src.data_ptr()
         si.sa_cos, si.sa_sin, si.ca_cos, si.ca_sin = (t.data_ptr() for t in (sa_cos, sa_sin, ca_cos, ca_sin))
         si.T, si.n_steps, si.action_dim = T, n_steps, int(action_dim)
+        if kv_ready is not None:
+            if kv_ready.dtype != torch.int32 or kv_ready.numel() < self.L or kv_ready.device != self.device:
+                raise ValueError(f"kv_ready must be an int32 tensor of >= {self.L} values on the expert's device")
+            si.kv_ready, si.kv_ready_value = kv_ready.data_ptr(), int(kv_ready_value)
         si.trace_h = trace.data_ptr() if trace is not None else None
         if prof is not None:
             need = self.nprog * (1 + self.barriers(n_steps))
             if prof.dtype != torch.int64 or prof.numel() < need or not prof.is_contiguous():
                 raise ValueError(f"prof must be a contiguous int64 tensor of >= {need} elements")
             si.prof = prof.data_ptr()
-        stream = torch.cuda.current_stream(self.device).cuda_stream
-        _lib.check(self._lib.mkx_run(self._h, C.byref(si), C.c_void_p(stream)), "mkx_run")
-        return out.reshape(1, T, self.A)
+        keep = (x_in, mods, dt_t, sa_cos, sa_sin, ca_cos, ca_sin, cu_kv, cu_src)
+        return si, out.reshape(1, T, self.A), keep
+
+    def run_from_host(self, x_t: torch.Tensor, mods: torch.Tensor, dt, past, action_dim: int) -> torch.Tensor:
+        """``run`` with every input in pinned host memory (``past`` as for ``run``, its tensors on the
+        host; dt a float or a one-element tensor). Returns the device result like ``run``.
+
+        On the current stream the small inputs (x_t, mods, dt, RoPE tables, cu_kv, cu_src) are copied
+        in; on a side stream that first waits for this handle's previous launch (it read the same
+        buffers), per layer the memory and cross-attention K/V and a 4-byte readiness word, all plain
+        host-to-device copies issued by the library (a kernel on that stream would wait for the SMs
+        the launch holds); then the launch is enqueued on the current stream. The launch waits for
+        layer l's word before reading its K/V, so the K/V copies run under the first Euler step
+        instead of ahead of the launch. The host tensors must stay alive until the streams have used
+        them."""
+        dev = self.device
+        st = past.register_step
+        host = {"x": x_t, "mods": mods, "sa_cos": st["sa_pe"][0], "sa_sin": st["sa_pe"][1],
+                "ca_cos": st["ca_pe"][0], "ca_sin": st["ca_pe"][1], "cu_kv": st["cu_kv"], "cu_src": st["cu_src"]}
+        if isinstance(dt, torch.Tensor):
+            host["dt"] = dt.reshape(-1)[:1]
+        if len(st["mem_kv"]) != self.L or len(past.cross_attn_kv) != self.L:
+            raise ValueError("need one memory and one cross-attention K/V pair per layer")
+        kv = [(m[0], m[1], c[0], c[1]) for m, c in zip(st["mem_kv"], past.cross_attn_kv)]
+        storages = {}
+        for t in list(host.values()) + [x for layer in kv for x in layer]:
+            if t.device.type != "cpu" or not t.is_contiguous():
+                raise ValueError("run_from_host takes contiguous host tensors")
+            storages[t.untyped_storage().data_ptr()] = t
+        if not all(t.is_pinned() for t in storages.values()):
+            raise ValueError("run_from_host takes tensors in pinned host memory")
+        key = tuple((k, tuple(v.shape), v.dtype) for k, v in host.items()) + tuple(
+            (tuple(t.shape), t.dtype) for layer in kv for t in layer)
+        b = getattr(self, "_host_bufs", None)
+        if b is None or b["key"] != key:
+            b = {"key": key,
+                 "in": {k: torch.empty(v.shape, dtype=v.dtype, device=dev) for k, v in host.items()},
+                 "kv": [tuple(torch.empty(t.shape, dtype=t.dtype, device=dev) for t in layer) for layer in kv],
+                 "ready": torch.zeros(self.L, dtype=torch.int32, device=dev),
+                 "ring": torch.zeros((64, self.L), dtype=torch.int32).pin_memory(),
+                 "ring_done": [None] * 64, "seq": 0,
+                 "copy": torch.cuda.Stream(dev), "prev": None}
+            self._host_bufs = b
+            # the buffers were created (zeroed) on the current stream: the side stream's first
+            # copies must not overtake that
+            b["copy"].wait_stream(torch.cuda.current_stream(dev))
+        main = torch.cuda.current_stream(dev)
+        self._h2d([(b["in"][k], v) for k, v in host.items()], main)
+        b["seq"] += 1
+        value = b["seq"] & 0x3FFFFFFF or 1  # never the buffer's initial 0
+        slot = b["seq"] % 64
+        if b["ring_done"][slot] is not None:
+            b["ring_done"][slot].synchronize()  # that slot's words were copied out 64 calls ago
+        row = b["ring"][slot]
+        row.fill_(value)
+        cs = b["copy"]
+        if b["prev"] is not None:
+            cs.wait_event(b["prev"])  # the previous launch has finished with the buffers
+        pairs = []
+        for l in range(self.L):
+            pairs += list(zip(b["kv"][l], kv[l]))
+            pairs.append((b["ready"][l:l + 1], row[l:l + 1]))
+        self._h2d(pairs, cs)  # enqueued before the launch: the copies start while it is prepared
+        ev = torch.cuda.Event()
+        ev.record(cs)
+        if b.get("si") is None or b["dt_key"] != (None if "dt" in host else float(dt)):
+            # the device buffers never change for this buffer set: validate and describe them once
+            d = b["in"]
+            dpast = SimpleNamespace(
+                register_step={"mem_kv": [(b["kv"][l][0], b["kv"][l][1]) for l in range(self.L)],
+                               "sa_pe": (d["sa_cos"], d["sa_sin"]), "ca_pe": (d["ca_cos"], d["ca_sin"]),
+                               "cu_kv": d["cu_kv"], "cu_src": d["cu_src"]},
+                cross_attn_kv=[(b["kv"][l][2], b["kv"][l][3]) for l in range(self.L)])
+            b["si"], _, b["si_keep"] = self._step_inputs(d["x"], d["mods"], d["dt"] if "dt" in d else dt, dpast,
+                                                         action_dim, None, None, b["ready"], value)
+            b["dt_key"] = None if "dt" in host else float(dt)
+            si = b["si"]
+            direct = {"x": si.x_in, "mods": si.mods, "sa_cos": si.sa_cos, "sa_sin": si.sa_sin, "ca_cos": si.ca_cos,
+                      "ca_sin": si.ca_sin, "cu_kv": si.cu_kv, "cu_src": si.cu_src}
+            if any(d[k].data_ptr() != v for k, v in direct.items()) or ("dt" in d and d["dt"].data_ptr() != si.dt):
+                b["si"] = None
+                raise ValueError("run_from_host needs inputs that need no conversion: x_t and tables fp32, "
+                                 "mods bf16 or fp32, cu_kv / cu_src int32, dt fp32")
+        si = b["si"]
+        if not 1 <= int(action_dim) <= AO:
+            raise ValueError(f"action_dim={action_dim} must be in 1..{AO}")
+        out = torch.empty((1, int(si.T), self.A), dtype=torch.float32, device=dev)
+        si.x_out, si.action_dim, si.kv_ready_value = out.data_ptr(), int(action_dim), int(value)
+        self._launch(si)
+        done = torch.cuda.Event()
+        done.record(main)
+        b["ring_done"][slot] = ev
+        b["prev"] = done
+        return out
+
+    def _h2d(self, pairs, stream) -> None:
+        """Host-to-device copies (dst, src) in order on `stream`, one library call for all."""
+        n = len(pairs)
+        dst = (C.c_void_p * n)(*[dd.data_ptr() for dd, _ in pairs])
+        src = (C.c_void_p * n)(*[ss.data_ptr() for _, ss in pairs])
+        nb = (C.c_size_t * n)(*[ss.numel() * ss.element_size() for _, ss in pairs])
+        _lib.check(self._lib.mkx_h2d_copies(n, dst, src, nb, C.c_void_p(stream.cuda_stream)), "mkx_h2d_copies")
 
     def barriers(self, n_steps: int) -> int:
         return int(self._lib.mkx_sync_points(self._h, int(n_steps)))

@@ -17,7 +17,7 @@ def declared_symbols():
     syms = set()
     for h in HEADERS:
         text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
-        syms |= set(re.findall(r"\b(mkx_[a-z_]+)\s*\(", text))
+        syms |= set(re.findall(r"\b(mkx_[a-z0-9_]+)\s*\(", text))
     return sorted(syms)
 
 
@@ -32,7 +32,7 @@ def test_library_exports_every_declared_symbol():
     nm = shutil.which("nm")
     if nm:
         out = subprocess.run([nm, "-D", "--defined-only", str(_lib.lib_path())], capture_output=True, text=True).stdout
-        exported = set(re.findall(r"\b(mkx_[a-z_]+)\b", out))
+        exported = set(re.findall(r"\b(mkx_[a-z0-9_]+)\b", out))
         assert set(syms) <= exported
 
 
@@ -114,3 +114,11 @@ def test_modulation_arguments_are_rejected_without_a_device():
     assert lib.mkx_mods_input(None, None, None) == _lib.MKX_ERR_INVALID_ARG
     assert lib.mkx_mods_last_error(None, None) == _lib.MKX_ERR_INVALID_ARG
     lib.mkx_mods_destroy(None)
+
+
+def test_host_copy_arguments_are_checked_without_a_device():
+    from reki_megakernel_b200 import _lib
+    lib = _lib.load()
+    assert lib.mkx_h2d_copies(-1, None, None, None, None) == _lib.MKX_ERR_INVALID_ARG
+    assert lib.mkx_h2d_copies(2, None, None, None, None) == _lib.MKX_ERR_INVALID_ARG
+    assert lib.mkx_h2d_copies(0, None, None, None, None) == _lib.MKX_OK   # nothing to copy
