@@ -211,15 +211,19 @@ class ExpertMegakernel:
         if len(st["mem_kv"]) != self.L or len(past.cross_attn_kv) != self.L:
             raise ValueError("need one memory and one cross-attention K/V pair per layer")
         kv = [(m[0], m[1], c[0], c[1]) for m, c in zip(st["mem_kv"], past.cross_attn_kv)]
-        storages = {}
-        for t in list(host.values()) + [x for layer in kv for x in layer]:
-            if t.device.type != "cpu" or not t.is_contiguous():
-                raise ValueError("run_from_host takes contiguous host tensors")
-            storages[t.untyped_storage().data_ptr()] = t
-        if not all(t.is_pinned() for t in storages.values()):
-            raise ValueError("run_from_host takes tensors in pinned host memory")
+        tensors = list(host.values()) + [x for layer in kv for x in layer]
         key = tuple((k, tuple(v.shape), v.dtype) for k, v in host.items()) + tuple(
             (tuple(t.shape), t.dtype) for layer in kv for t in layer)
+        seen = (key, tuple(t.data_ptr() for t in tensors), tuple(t.stride() for t in tensors))
+        if seen != getattr(self, "_host_seen", None):  # the same host tensors as last call: checked then
+            storages = {}
+            for t in tensors:
+                if t.device.type != "cpu" or not t.is_contiguous():
+                    raise ValueError("run_from_host takes contiguous host tensors")
+                storages[t.untyped_storage().data_ptr()] = t
+            if not all(t.is_pinned() for t in storages.values()):
+                raise ValueError("run_from_host takes tensors in pinned host memory")
+            self._host_seen = seen
         b = getattr(self, "_host_bufs", None)
         if b is None or b["key"] != key:
             b = {"key": key,
