@@ -42,6 +42,16 @@ def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+READY_PERIOD = 0x3FFFFFFF
+
+
+def ready_value(seq: int) -> int:
+    """The readiness-word value of ``run_from_host`` call ``seq`` (1, 2, ...): cycles through
+    1..READY_PERIOD, so it is never the buffer's initial 0 and never the previous call's value (the
+    launch would otherwise take the previous call's words for this call's K/V)."""
+    return (seq - 1) % READY_PERIOD + 1
+
+
 class ExpertMegakernel:
     """Packs the expert weights once; ``run`` integrates Euler steps 2..N in one launch."""
 
@@ -200,8 +210,9 @@ class ExpertMegakernel:
         host-to-device copies issued by the library (a kernel on that stream would wait for the SMs
         the launch holds); then the launch is enqueued on the current stream. The launch waits for
         layer l's word before reading its K/V, so the K/V copies run under the first Euler step
-        instead of ahead of the launch. The host tensors must stay alive until the streams have used
-        them."""
+        instead of ahead of the launch. Successive calls may come from different current streams:
+        each call's copies wait for the previous call's launch. The host tensors must stay alive
+        until the streams have used them."""
         dev = self.device
         st = past.register_step
         host = {"x": x_t, "mods": mods, "sa_cos": st["sa_pe"][0], "sa_sin": st["sa_pe"][1],
@@ -232,15 +243,17 @@ class ExpertMegakernel:
                  "ready": torch.zeros(self.L, dtype=torch.int32, device=dev),
                  "ring": torch.zeros((64, self.L), dtype=torch.int32).pin_memory(),
                  "ring_done": [None] * 64, "seq": 0,
-                 "copy": torch.cuda.Stream(dev), "prev": None}
+                 "copy": torch.cuda.Stream(dev), "prev": None, "prev_stream": None}
             self._host_bufs = b
             # the buffers were created (zeroed) on the current stream: the side stream's first
             # copies must not overtake that
             b["copy"].wait_stream(torch.cuda.current_stream(dev))
         main = torch.cuda.current_stream(dev)
+        if b["prev"] is not None and b["prev_stream"] != main:
+            main.wait_event(b["prev"])  # the previous launch, on another stream, still reads b["in"]
         self._h2d([(b["in"][k], v) for k, v in host.items()], main)
         b["seq"] += 1
-        value = b["seq"] & 0x3FFFFFFF or 1  # never the buffer's initial 0
+        value = ready_value(b["seq"])
         slot = b["seq"] % 64
         if b["ring_done"][slot] is not None:
             b["ring_done"][slot].synchronize()  # that slot's words were copied out 64 calls ago
@@ -283,7 +296,7 @@ class ExpertMegakernel:
         done = torch.cuda.Event()
         done.record(main)
         b["ring_done"][slot] = ev
-        b["prev"] = done
+        b["prev"], b["prev_stream"] = done, main
         return out
 
     def _h2d(self, pairs, stream) -> None:

@@ -122,3 +122,15 @@ def test_host_copy_arguments_are_checked_without_a_device():
     assert lib.mkx_h2d_copies(-1, None, None, None, None) == _lib.MKX_ERR_INVALID_ARG
     assert lib.mkx_h2d_copies(2, None, None, None, None) == _lib.MKX_ERR_INVALID_ARG
     assert lib.mkx_h2d_copies(0, None, None, None, None) == _lib.MKX_OK   # nothing to copy
+
+
+def test_readiness_values_never_repeat_consecutively():
+    """``run_from_host`` tells its launch which readiness-word value marks this call's K/V: it must
+    differ from the zero the words start at and from the previous call's value, across the wrap."""
+    from reki_megakernel_b200.mk_expert import READY_PERIOD, ready_value
+    seqs = [1, 2, 3, READY_PERIOD - 1, READY_PERIOD, READY_PERIOD + 1, READY_PERIOD + 2, 2 * READY_PERIOD + 1]
+    vals = [ready_value(s) for s in seqs]
+    assert vals[:3] == [1, 2, 3] and vals[4:7] == [READY_PERIOD, 1, 2]
+    assert all(1 <= v <= READY_PERIOD < 2 ** 31 for v in vals)
+    for s in [1, READY_PERIOD - 1, READY_PERIOD, READY_PERIOD + 1, 5 * READY_PERIOD]:
+        assert ready_value(s + 1) != ready_value(s)

@@ -73,3 +73,26 @@ def test_missing_readiness_word_times_out_and_recovers(full):
     torch.cuda.synchronize()
     mk.check_device_error()
     assert torch.equal(again, good)
+
+
+def test_run_from_host_on_alternating_streams(full):
+    """Successive calls from two different current streams: each call's input copies must wait for
+    the previous launch, which ran on the other stream and reads the same device buffers."""
+    dims, mk = full
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    cases = [make_inputs(dims, S=160, seed=20 + i, noise_seed=200 + i) for i in range(4)]
+    wants = []
+    for inp in cases:
+        d = inp.to(DEV)
+        wants.append(mk.run(d.x[:1], d.mods[0], d.dt[:1], make_past(d), d.action_dim).clone())
+    torch.cuda.synchronize()
+    hosts = [(inp.x[:1].contiguous().pin_memory(), inp.mods[0].contiguous().pin_memory(),
+              inp.dt[:1].contiguous().pin_memory(), _pinned_past(inp), inp.action_dim) for inp in cases]
+    gots = []
+    for i, h in enumerate(hosts):
+        with torch.cuda.stream(streams[i % 2]):
+            gots.append(mk.run_from_host(*h))
+    torch.cuda.synchronize()
+    mk.check_device_error()
+    for got, want in zip(gots, wants):
+        assert torch.equal(got, want)
