@@ -161,8 +161,16 @@ class ExpertMegakernel:
             return t.float().contiguous() if t.dtype != torch.float32 else t.contiguous()
         sa_cos, sa_sin = (pe(t) for t in step["sa_pe"])
         ca_cos, ca_sin = (pe(t) for t in step["ca_pe"])
-        cu_kv = step["cu_kv"].to(torch.int32) if step["cu_kv"].dtype != torch.int32 else step["cu_kv"]
-        cu_src = step["cu_src"].to(torch.int32) if step["cu_src"].dtype != torch.int32 else step["cu_src"]
+        cu_kv = step["cu_kv"].to(torch.int32).contiguous()
+        cu_src = step["cu_src"].to(torch.int32).contiguous()
+        if cu_kv.numel() < 2 or cu_src.numel() < 2:
+            raise ValueError("cu_kv and cu_src need two values each")
+        # the library sees only pointers: a tensor on another device would be read through a bad address
+        placed = (("x_t", x_t), ("mods", mods), ("sa_pe", sa_cos), ("sa_pe", sa_sin), ("ca_pe", ca_cos),
+                  ("ca_pe", ca_sin), ("cu_kv", cu_kv), ("cu_src", cu_src))
+        for name, t in placed:
+            if t.device != self.device:
+                raise ValueError(f"{name} must be on the expert's device {self.device}, got {t.device}")
         x_in = x_t.reshape(T, self.A)
         x_in = x_in.float().contiguous() if x_in.dtype != torch.float32 else x_in.contiguous()
         if mods.dtype not in (torch.bfloat16, torch.float32):

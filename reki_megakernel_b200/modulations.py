@@ -19,6 +19,22 @@ from .synthetic import ModulationWeights
 NMAX = 16
 
 
+def check_out(MODW: int, device, num_steps: int, out) -> None:
+    """What ``StepModulations.run`` checks of caller-owned outputs before it hands their pointers to
+    the library, which cannot see sizes or devices: mods a contiguous [N, MODW] bf16 tensor and dt a
+    float32 tensor of at least one value, both on ``device``. Raises ValueError."""
+    if out is None:
+        return
+    if len(out) != 2:
+        raise ValueError("out must be a (mods, dt) pair")
+    mods, dt = out
+    if (mods.device != device or mods.dtype != torch.bfloat16 or tuple(mods.shape) != (num_steps, MODW)
+            or not mods.is_contiguous()):
+        raise ValueError(f"out mods must be a contiguous [{num_steps}, {MODW}] bf16 tensor on {device}")
+    if dt.device != device or dt.dtype != torch.float32 or dt.numel() < 1:
+        raise ValueError(f"out dt must be a float32 tensor of at least one value on {device}")
+
+
 class StepModulations:
     """``StepModulations(weights)(num_steps, state) -> (mods [N, MODW] bf16, dt [1] fp32)`` on the
     weights' device."""
@@ -56,9 +72,8 @@ class StepModulations:
             mods = torch.empty((num_steps, self.MODW), dtype=torch.bfloat16, device=self.device)
             dt = torch.empty((1,), dtype=torch.float32, device=self.device)
         else:
+            check_out(self.MODW, self.device, num_steps, out)
             mods, dt = out
-            if mods.shape != (num_steps, self.MODW) or not mods.is_contiguous() or mods.dtype != torch.bfloat16:
-                raise ValueError("out mods must be a contiguous [N, MODW] bf16 tensor")
         st = self.lib.mkx_mods_run(self.h, num_steps, state.data_ptr(), mods.data_ptr(), dt.data_ptr(),
                                    torch.cuda.current_stream(self.device).cuda_stream)
         _lib.check(st, "mkx_mods_run")

@@ -16,6 +16,24 @@ from . import _lib
 from .synthetic import PrepareWeights, rope_cos_sin
 
 
+def check_run_args(dims, device, S: int, SP: int, cos: torch.Tensor, sin: torch.Tensor, out) -> None:
+    """What ``RegisterPrepare.run`` checks before it hands raw pointers to the library, which cannot
+    see sizes or devices: SP >= S, RoPE tables [>= S, HD] fp32 and, when given, the outputs
+    [L, SP, NH, HD] bf16, all contiguous on ``device``. Raises ValueError."""
+    if SP < S:
+        raise ValueError(f"SP={SP} must be >= S={S}")
+    for name, t in (("cos", cos), ("sin", sin)):
+        if t.device != device or t.dtype != torch.float32 or t.dim() != 2 or t.shape[0] < S or t.shape[1] != dims.HD:
+            raise ValueError(f"{name} must be [>= {S}, {dims.HD}] fp32 on {device}")
+    if out is not None:
+        shape = (dims.L, SP, dims.NH, dims.HD)
+        if len(out) != 2:
+            raise ValueError("out must be a (k, v) pair")
+        for name, t in zip(("k", "v"), out):
+            if t.device != device or t.dtype != torch.bfloat16 or tuple(t.shape) != shape or not t.is_contiguous():
+                raise ValueError(f"out {name} must be a contiguous {list(shape)} bf16 tensor on {device}")
+
+
 class RegisterPrepare:
     """``RegisterPrepare(weights).run(src) -> (k, v)``, both [L, SP, NH, HD] bf16 on src's device."""
 
@@ -55,6 +73,7 @@ class RegisterPrepare:
         SP = SP or S
         if cos is None or sin is None:
             cos, sin = self.tables(S)
+        check_run_args(d, self.device, S, SP, cos, sin, out)
         if out is None:
             k = torch.empty((d.L, SP, d.NH, d.HD), dtype=torch.bfloat16, device=self.device)
             v = torch.empty_like(k)

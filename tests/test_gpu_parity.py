@@ -153,6 +153,36 @@ def test_fp32_mods_bitwise_equal(small):
     assert torch.equal(a, b)
 
 
+@pytest.mark.parametrize("where", ["x_t", "mods", "dt", "sa_pe", "ca_pe", "cu_kv", "cu_src", "mem_kv", "cross_kv"])
+def test_host_tensors_are_rejected_before_launch(small, where):
+    """Every tensor ``run`` hands to the library by pointer must be on the expert's device: one left
+    in host memory raises ValueError and nothing is launched; the next correct call still matches."""
+    dims, w, mk, _ = small
+    inp = make_inputs(dims, seed=13)
+    good = run_mk(mk, inp)
+    d = inp.to(DEV)
+    past = make_past(d)
+    x, mods, dt = d.x[:1], d.mods[0], d.dt[:1]
+    st = past.register_step
+    if where == "x_t":
+        x = x.cpu()
+    elif where == "mods":
+        mods = mods.cpu()
+    elif where == "dt":
+        dt = dt.cpu()
+    elif where in ("sa_pe", "ca_pe"):
+        st[where] = tuple(t.cpu() for t in st[where])
+    elif where in ("cu_kv", "cu_src"):
+        st[where] = st[where].cpu()
+    elif where == "mem_kv":
+        st["mem_kv"] = [(k.cpu(), v) for k, v in st["mem_kv"]]
+    else:
+        past.cross_attn_kv = [(k, v.cpu()) for k, v in past.cross_attn_kv]
+    with pytest.raises(ValueError):
+        mk.run(x, mods, dt, past, d.action_dim)
+    assert torch.equal(run_mk(mk, inp), good)
+
+
 def test_deterministic_and_repeatable(small):
     dims, w, mk, _ = small
     inp = make_inputs(dims, seed=11)
