@@ -174,9 +174,21 @@ __device__ __forceinline__ void trace_point(const Params& p, const Cta& c, int p
     p.prof[(size_t)c.G * per_cta + (c.cta == 0 ? 0 : per_cta * 8) + (size_t)c.stages * 8 + pt] = globaltimer();
   }
 }
+// The stamp taken only once `dep` is computed (a plain stamp may be scheduled ahead of the work it
+// follows in the source).
+__device__ __forceinline__ void trace_point_after(const Params& p, const Cta& c, int pt, uint32_t dep) {
+  if (p.prof != nullptr && c.tid == 0 && (c.cta == 0 || c.cta == 100)) {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t) : "r"(dep) : "memory");
+    const size_t per_cta = 2 + (size_t)p.n_steps * (8 * p.L + 1);
+    p.prof[(size_t)c.G * per_cta + (c.cta == 0 ? 0 : per_cta * 8) + (size_t)c.stages * 8 + pt] = t;
+  }
+}
 #define MKX_TRACE(pt) trace_point(p, c, pt)
+#define MKX_TRACE_AFTER(pt, dep) trace_point_after(p, c, pt, dep)
 #else
 #define MKX_TRACE(pt) ((void)0)
+#define MKX_TRACE_AFTER(pt, dep) ((void)0)
 #endif
 
 // Optional timeline: thread 0 of every CTA stamps %globaltimer at the launch start (index 0) and at
@@ -270,7 +282,10 @@ __device__ __forceinline__ void consumed(const Params& p, Cta& c, int b) {
 
 // Exchange polls. issue_pairs loads N 16-byte pairs of words at addr(i) (entries outside `valid`
 // count as fresh); complete_pairs re-polls the stale ones until both tags of every pair equal `tag`.
-// Addresses are recomputed rather than held, to keep registers for the data.
+// Each round checks every pair first and then reissues all stale ones together (reissuing each
+// stale pair as soon as it was checked was 1 % slower per predict); no pause between rounds (a
+// 128 ns __nanosleep made the predict 50 % slower). Addresses are recomputed rather than held, to
+// keep registers for the data.
 // Returns 0, or the Waiter code (1 timeout, 2 abort seen).
 template <int N, typename Addr>
 __device__ __forceinline__ void issue_pairs(Addr addr, u64 (&w0)[N], u64 (&w1)[N], uint32_t valid, uint32_t tag) {
@@ -289,15 +304,14 @@ __device__ __forceinline__ int complete_pairs(Addr addr, u64 (&w0)[N], u64 (&w1)
   while (true) {
     uint32_t bad = 0;
 #pragma unroll
-    for (int i = 0; i < N; ++i) {
-      if (tag_of(w0[i]) != tag || tag_of(w1[i]) != tag) {
-        bad |= 1u << i;
-        ld_volatile_v2(addr(i), w0[i], w1[i]);
-      }
-    }
+    for (int i = 0; i < N; ++i)
+      if (tag_of(w0[i]) != tag || tag_of(w1[i]) != tag) bad |= 1u << i;
     if (bad == 0u) return 0;
     const int r = wt.tick();
     if (r) return r;
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+      if ((bad >> i) & 1u) ld_volatile_v2(addr(i), w0[i], w1[i]);
   }
 }
 __device__ __forceinline__ int poll_word(const u64* ptr, u64& w, uint32_t tag, Waiter& wt) {
@@ -341,6 +355,7 @@ __device__ int stage_rows_adarms(const Params& p, Cta& c, const u64* rows, uint3
     Waiter wt(p.status, p.timeout_ns);
     issue_pairs<SPAIRS>(addr, w0, w1, live ? (1u << SPAIRS) - 1u : 0u, tag);
     r = complete_pairs<SPAIRS>(addr, w0, w1, tag, wt);
+    MKX_TRACE_AFTER(6, (uint32_t)w0[SPAIRS - 1] ^ (uint32_t)w1[SPAIRS - 1]);
   } else {
 #pragma unroll
     for (int j = 0; j < SPAIRS; ++j) {
@@ -364,9 +379,13 @@ __device__ int stage_rows_adarms(const Params& p, Cta& c, const u64* rows, uint3
   float ss = (s4[0] + s4[1]) + (s4[2] + s4[3]);
 #pragma unroll
   for (int o = SROW / 2; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (rows != nullptr) MKX_TRACE_AFTER(4, __float_as_uint(ss));
   const float rstd = rsqrtf(ss / (float)H + p.eps);
   const ModT* msh = msc + H;
   float* res = cRes(p, c) + n * RESW;
+  // All modulation loads and arithmetic first, then all stores: a store to X could alias a later
+  // modulation load (both shared memory), so interleaved they serialise load -> store -> load.
+  uint32_t outv[2 * SPAIRS];
 #pragma unroll
   for (int j = 0; j < 2 * SPAIRS; ++j) {  // column pairs (ca, ca+1) then (ca+8, ca+9) of word pair j / 2
     const int col = col_a_of(part + SROW * (j >> 1)) + 8 * (j & 1);
@@ -375,10 +394,18 @@ __device__ int stage_rows_adarms(const Params& p, Cta& c, const u64* rows, uint3
     const float2 sc = mod2<ModT>(msc, col), sh = mod2<ModT>(msh, col);
     const float a0 = fmaf(h0 * rstd, 1.f + sc.x, sh.x);
     const float a1 = fmaf(h1 * rstd, 1.f + sc.y, sh.y);
-    *reinterpret_cast<uint32_t*>(xrow + col * 2) = live ? pack_bf2(a0, a1) : 0u;
+    outv[j] = live ? pack_bf2(a0, a1) : 0u;
+  }
+  if (rows != nullptr) MKX_TRACE_AFTER(1, outv[2 * SPAIRS - 1] ^ outv[0]);
+#pragma unroll
+  for (int j = 0; j < 2 * SPAIRS; ++j) {
+    const int col = col_a_of(part + SROW * (j >> 1)) + 8 * (j & 1);
+    *reinterpret_cast<uint32_t*>(xrow + col * 2) = outv[j];
     // c0 and R_h are even: a column pair is entirely inside or outside the residual columns
-    if (live && (unsigned)(col - c.c0) < (unsigned)c.R_h)
-      *reinterpret_cast<float2*>(res + (col - c.c0)) = make_float2(h0, h1);
+    if (live && (unsigned)(col - c.c0) < (unsigned)c.R_h) {
+      const uint32_t u = payload_of((j & 1) ? w1[j >> 1] : w0[j >> 1]);
+      *reinterpret_cast<float2*>(res + (col - c.c0)) = make_float2(bf_lo(u), bf_hi(u));
+    }
   }
   return fail_code(p, c, r, stage);
 }
@@ -1008,7 +1035,7 @@ __device__ __forceinline__ int stage_norm_gemm(const Params& p, Cta& c, int whic
                       : xb[which == 1 ? B_H2 : B_H3] + (size_t)par * TP * HWORDS;
   fail |= stage_rows_adarms<ModT>(p, c, rows, which == 0 ? tag - 1u : tag, ST_QKV + 3 * which,
                                   mods_slot<ModT>(p, c, q));
-  MKX_TRACE(0);
+  MKX_TRACE_AFTER(0, (uint32_t)fail);
   const int slot = which == 0 ? S_QKV : (which == 1 ? S_QCA : S_GU);
   fail |= !wait_bar(p, c, slot);
   if (__syncthreads_or(fail)) return 1;
@@ -1020,7 +1047,6 @@ __device__ __forceinline__ int stage_norm_gemm(const Params& p, Cta& c, int whic
   __syncthreads();
   MKX_TRACE(3);
   if (c.tid == ISSUER && gi + 1 < p.n_steps * p.L) issue_slot(p, c, slot, (gi + 1) % p.L);
-  MKX_TRACE(4);
   if (which == 2) {
     epi_gu(p, c, xb[B_G] + (size_t)par * TP * (p.I >> 1), tag);
   } else if (which == 1) {
