@@ -349,6 +349,18 @@ __device__ int stage_rows_adarms(const Params& p, Cta& c, const u64* rows, uint3
   const bool live = n < p.T;
   u64 w0[SPAIRS], w1[SPAIRS];
   int r = 0;
+  // bf16 modulation pairs of this thread's columns, read before the polls go out: once they are in
+  // flight, a shared-memory load waits behind the CTA's outstanding exchange loads (1.4 % per
+  // predict). fp32 rows would need twice the registers and are read in the loop below.
+  uint32_t msr[2 * SPAIRS], mhr[2 * SPAIRS];
+  if constexpr (sizeof(ModT) == 2) {
+#pragma unroll
+    for (int j = 0; j < 2 * SPAIRS; ++j) {
+      const int col = col_a_of(part + SROW * (j >> 1)) + 8 * (j & 1);
+      msr[j] = *reinterpret_cast<const uint32_t*>(msc + col);
+      mhr[j] = *reinterpret_cast<const uint32_t*>(msc + H + col);
+    }
+  }
   if (rows != nullptr) {
     const u64* base = rows + (size_t)n * HWORDS + 2 * part;
     auto addr = [base](int j) { return base + 2 * SROW * j; };
@@ -391,7 +403,14 @@ __device__ int stage_rows_adarms(const Params& p, Cta& c, const u64* rows, uint3
     const int col = col_a_of(part + SROW * (j >> 1)) + 8 * (j & 1);
     const uint32_t u = payload_of((j & 1) ? w1[j >> 1] : w0[j >> 1]);
     const float h0 = bf_lo(u), h1 = bf_hi(u);
-    const float2 sc = mod2<ModT>(msc, col), sh = mod2<ModT>(msh, col);
+    float2 sc, sh;
+    if constexpr (sizeof(ModT) == 2) {
+      sc = make_float2(bf_lo(msr[j]), bf_hi(msr[j]));
+      sh = make_float2(bf_lo(mhr[j]), bf_hi(mhr[j]));
+    } else {
+      sc = mod2<ModT>(msc, col);
+      sh = mod2<ModT>(msh, col);
+    }
     const float a0 = fmaf(h0 * rstd, 1.f + sc.x, sh.x);
     const float a1 = fmaf(h1 * rstd, 1.f + sc.y, sh.y);
     outv[j] = live ? pack_bf2(a0, a1) : 0u;
@@ -508,7 +527,19 @@ __device__ int mma_from_words(const Params& p, Cta& c, const char* wslot, int R,
     issue_pairs<2 * CH>([base, d1off](int i) { return base + (i >> 1) * 8 + ((i & 1) ? d1off : 0); }, b.w0, b.w1,
                         valid, tag);
   };
-  auto consume = [&](WordChunk<CH>& b, int ch) -> int {
+  // Weight fragments of two chunks, read before their polls go out (a shared-memory load issued
+  // behind outstanding exchange loads waits for them).
+  uint2 ap0[CH], bp0[CH], ap1[CH], bp1[CH];
+  auto prefetch = [&](uint2 (&ap)[CH], uint2 (&bp)[CH], int ch) {
+#pragma unroll
+    for (int i = 0; i < CH; ++i) {
+      const int kb = kb0 + ch * CH + i;
+      const char* blk = A + (size_t)kb * R * 32;
+      ap[i] = (kb < kb1 && va) ? lds64(blk + g * 32) : make_uint2(0u, 0u);
+      bp[i] = (kb < kb1 && vb) ? lds64(blk + (g + 8) * 32) : make_uint2(0u, 0u);
+    }
+  };
+  auto consume = [&](WordChunk<CH>& b, int ch, const uint2 (&ap)[CH], const uint2 (&bp)[CH]) -> int {
     const int kbase = kb0 + ch * CH;
     const u64* base = row0 + kbase * 8;
     int rc = complete_pairs<2 * CH>([base, d1off](int i) { return base + (i >> 1) * 8 + ((i & 1) ? d1off : 0); },
@@ -518,9 +549,7 @@ __device__ int mma_from_words(const Params& p, Cta& c, const char* wslot, int R,
     for (int i = 0; i < CH; ++i) {
       const int kb = kbase + i;
       if (kb < kb1) {
-        const char* blk = A + (size_t)kb * R * 32;
-        const uint2 a = va ? lds64(blk + g * 32) : make_uint2(0u, 0u);
-        const uint2 bb = vb ? lds64(blk + (g + 8) * 32) : make_uint2(0u, 0u);
+        const uint2 a = ap[i], bb = bp[i];
         mma_bf16(d0, a.x, bb.x, a.y, bb.y, payload_of(b.w0[2 * i]), payload_of(b.w1[2 * i]));
         if (two) mma_bf16(d1, a.x, bb.x, a.y, bb.y, payload_of(b.w0[2 * i + 1]), payload_of(b.w1[2 * i + 1]));
       }
@@ -528,14 +557,20 @@ __device__ int mma_from_words(const Params& p, Cta& c, const char* wslot, int R,
     return 0;
   };
   int rc = 0;
+  prefetch(ap0, bp0, 0);
+  prefetch(ap1, bp1, 1);
   if (nch > 0) issue(buf0, 0);
   for (int ch = 0; ch < nch; ch += 2) {
     if (ch + 1 < nch) issue(buf1, ch + 1);
-    rc = consume(buf0, ch);
+    rc = consume(buf0, ch, ap0, bp0);
     if (rc || ch + 1 >= nch) break;
-    if (ch + 2 < nch) issue(buf0, ch + 2);
-    rc = consume(buf1, ch + 1);
+    if (ch + 2 < nch) {
+      prefetch(ap0, bp0, ch + 2);
+      issue(buf0, ch + 2);
+    }
+    rc = consume(buf1, ch + 1, ap1, bp1);
     if (rc) break;
+    if (ch + 3 < nch) prefetch(ap1, bp1, ch + 3);
   }
   store_partials(p, c, d0, d1);
   return fail_code(p, c, rc, stage);
