@@ -227,6 +227,71 @@ def run_timeline(args):
     print(json.dumps(out), flush=True)
 
 
+SUBSTAGE_POINTS = {
+    # numbered %globaltimer points inside each stage (thread 0 of the CTA), in the order they fire
+    "adarms_gemm": {6: "polls (thread 0's word pairs)", 4: "row sum of squares (the warp has its rows)",
+                    1: "AdaRMS arithmetic", 0: "X written", 2: "weight slot wait + barrier",
+                    3: "MMA + barrier", 5: "epilogue (publish)", 7: "stage end"},
+    "attention": {1: "polls (query, own k/v)", 3: "norm/RoPE + scores + block max",
+                  2: "softmax + P.V", 4: "group shuffles + partials to shared", 5: "barrier",
+                  7: "final reduce + publish y"},
+    "words_gemm": {0: "weight slot wait", 1: "polls + MMA + barrier", 5: "gated-residual epilogue (publish)",
+                   6: "barrier", 7: "stage end"},
+    "down": {0: "weight slot wait", 1: "level 1: polls of g + MMA + barrier", 2: "level 1 partials published",
+             3: "level 2: polls of the group partials + barrier", 5: "sum + gated residual (publish h)",
+             6: "barrier", 7: "stage end"},
+}
+SUBSTAGE_FAMILY = {"qkv": "adarms_gemm", "ca_q": "adarms_gemm", "gate_up": "adarms_gemm", "sa": "attention",
+                   "ca": "attention", "o": "words_gemm", "ca_o": "words_gemm", "down": "down"}
+
+
+def run_substage(args):
+    """Sub-phases of every layer stage, from the profiling build of the kernel (``libmkx_trace.so``,
+    compiled with -DMKX_SUBSTAGE_TRACE): thread 0 of CTA 0 stamps %globaltimer at numbered points
+    inside each stage. Per stage and point, in the order the points fire: time since the previous
+    point, the first measured from the end of the last CTA in the previous stage; median over the
+    90 layer passes and the predicts. Not a bench line: the stamps add stores."""
+    from reki_megakernel_b200 import _lib
+    _lib.use_traced_build()
+    from reki_megakernel_b200.mk_expert import ExpertMegakernel
+    from reki_megakernel_b200.synthetic import ExpertDims, make_inputs, make_past, make_weights
+    dims = ExpertDims()
+    mk = ExpertMegakernel(weights=make_weights(dims, seed=0).to("cuda"))
+    inp = make_inputs(dims).to("cuda")
+    past = make_past(inp)
+    G, n = mk.nprog, inp.n_steps
+    per = 1 + mk.barriers(n)
+    prof = torch.zeros(G * per + 16 * per, dtype=torch.int64, device="cuda")  # stage ends + 2 CTAs x 8 points
+    acc, stage_us = {}, {}
+    for it in range(args.warmup + args.steps):
+        prof.zero_()
+        mk.run(inp.x[:1], inp.mods[0], inp.dt[:1], past, inp.action_dim, prof=prof)
+        torch.cuda.synchronize()
+        mk.check_device_error()
+        if it < args.warmup:
+            continue
+        a = prof.cpu()
+        last = a[:G * per].view(G, per).max(0).values  # [1 + stage]: end of the last CTA
+        sub = a[G * per: G * per + 8 * per].view(per, 8)  # CTA 0: [stage index][point]
+        for s in range(n):
+            for l in range(dims.L):
+                for k, name in enumerate(STAGE_NAMES):
+                    st = 1 + s * (8 * dims.L + 1) + 8 * l + k  # stages finished before this one
+                    t0 = int(last[st])
+                    for v, pt in sorted((int(sub[st, q]), q) for q in range(8) if int(sub[st, q]) != 0):
+                        acc.setdefault((name, pt), []).append((v - t0) / 1e3)
+                        t0 = v
+                    stage_us.setdefault(name, []).append(float(last[st + 1] - last[st]) / 1e3)
+    out = {}
+    for name in STAGE_NAMES:
+        pts = SUBSTAGE_POINTS[SUBSTAGE_FAMILY[name]]
+        order = [q for q in pts if (name, q) in acc]
+        out[name] = {"stage_us": round(statistics.median(stage_us[name]), 3),
+                     "points": [[pts[q], round(statistics.median(acc[(name, q)]), 3)] for q in order]}
+    print(json.dumps({"substage_us": out, "cta": 0, "predicts": args.steps,
+                      "config": "REKI expert steps 2-10, T=10, S=160, 64 memory rows, batch 1"}), flush=True)
+
+
 def run_predict(args):
     """The GPU half of one predict after Euler step 1 (BASELINE configs[2] without step 1 and the VLM):
     modulation rows, cross-attention K/V of all layers and Euler steps 2..N replayed as one CUDA graph
@@ -618,6 +683,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--max-ref-steps", type=int, default=60)
     ap.add_argument("--timeline", action="store_true", help="per-stage critical path of one predict, no bench line")
+    ap.add_argument("--substage", action="store_true",
+                    help="sub-phases of each stage from the traced profiling build, no bench line")
     ap.add_argument("--prepare", action="store_true", help="time register_prepare (cross-attention K/V), own JSON line")
     ap.add_argument("--mods", action="store_true", help="time the per-step modulation rows (_step_modulations), own JSON line")
     ap.add_argument("--predict", action="store_true",
@@ -627,10 +694,10 @@ def main():
         args.warmup = 3
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    if args.timeline or args.prepare or args.mods or args.predict:
+    if args.timeline or args.substage or args.prepare or args.mods or args.predict:
         if rank == 0:
-            (run_timeline if args.timeline else run_prepare if args.prepare else run_mods if args.mods
-             else run_predict)(args)
+            (run_timeline if args.timeline else run_substage if args.substage else run_prepare if args.prepare
+             else run_mods if args.mods else run_predict)(args)
         return
     if world > 1:
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")

@@ -83,8 +83,20 @@ SIGNATURES = {
 _LIB = None
 
 
+_TRACED = False
+
+
 def lib_path() -> Path:
-    return _build.LIB
+    return _build.TRACE_LIB if _TRACED else _build.LIB
+
+
+def use_traced_build() -> None:
+    """Make ``load`` use the sub-stage-traced profiling variant (``libmkx_trace.so``) instead of
+    ``libmkx.so``. Must be called before the first ``load`` in the process."""
+    global _TRACED
+    if _LIB is not None:
+        raise RuntimeError("the CUDA library is already loaded")
+    _TRACED = True
 
 
 def load(build_if_missing: bool = True) -> C.CDLL:
@@ -92,11 +104,11 @@ def load(build_if_missing: bool = True) -> C.CDLL:
     global _LIB
     if _LIB is not None:
         return _LIB
-    path = _build.LIB
+    path = _build.TRACE_LIB if _TRACED else _build.LIB
     if build_if_missing:
         try:
-            if _build.stale():
-                _build.build()
+            if _build.stale(path):
+                _build.build(traced=_TRACED)
         except RuntimeError:
             if not path.exists():
                 raise

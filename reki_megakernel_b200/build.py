@@ -1,6 +1,7 @@
 """Build recipe for the in-tree CUDA library ``libmkx.so`` (sm_100a only).
 
-    python -m reki_megakernel_b200.build
+    python -m reki_megakernel_b200.build             # libmkx.so
+    python -m reki_megakernel_b200.build --traced    # libmkx_trace.so (profiling variant)
 
 nvcc cross-compiles without a GPU; the library lands next to this file so it travels with the
 source tree and is the one ``reki_megakernel_b200._lib`` loads.
@@ -16,6 +17,9 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 LIB = PKG / "libmkx.so"
+# Profiling variant: the same sources with -DMKX_SUBSTAGE_TRACE (thread 0 of CTAs 0 and 100 stamps
+# %globaltimer at numbered points inside each stage); loaded only after _lib.use_traced_build().
+TRACE_LIB = PKG / "libmkx_trace.so"
 SOURCES = [PKG / "csrc" / "mk_expert.cu", PKG / "csrc" / "mk_prepare.cu", PKG / "csrc" / "mk_mods.cu"]
 HEADERS = [PKG / "csrc" / "mkx_device.cuh", ROOT / "include" / "mkx.h", ROOT / "include" / "mkx_prepare.h",
            ROOT / "include" / "mkx_mods.h"]
@@ -29,18 +33,21 @@ def nvcc() -> str:
     return cand
 
 
-def stale() -> bool:
-    if not LIB.exists():
+def stale(lib: Path | None = None) -> bool:
+    lib = lib or LIB
+    if not lib.exists():
         return True
-    t = LIB.stat().st_mtime
+    t = lib.stat().st_mtime
     return any(p.stat().st_mtime > t for p in SOURCES + HEADERS)
 
 
-def build(force: bool = False, verbose: bool = False) -> Path:
-    if not force and not stale():
-        return LIB
-    tmp = LIB.with_suffix(f".so.tmp{os.getpid()}")
+def build(force: bool = False, verbose: bool = False, traced: bool = False) -> Path:
+    lib = TRACE_LIB if traced else LIB
+    if not force and not stale(lib):
+        return lib
+    tmp = lib.with_suffix(f".so.tmp{os.getpid()}")
     cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
+           *(["-DMKX_SUBSTAGE_TRACE"] if traced else []),
            "-I", str(ROOT / "include"), "-I", str(PKG / "csrc"), "-o", str(tmp), *map(str, SOURCES)]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
@@ -49,9 +56,9 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         raise RuntimeError(f"nvcc failed ({r.returncode}):\n{r.stdout}\n{r.stderr}")
     if verbose:
         print(r.stderr, file=sys.stderr)
-    os.replace(tmp, LIB)
-    return LIB
+    os.replace(tmp, lib)
+    return lib
 
 
 if __name__ == "__main__":
-    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))
+    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv, traced="--traced" in sys.argv))

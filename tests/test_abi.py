@@ -5,6 +5,7 @@ import ctypes as C
 import re
 import shutil
 import subprocess
+import sys
 
 import pytest
 
@@ -134,3 +135,26 @@ def test_readiness_values_never_repeat_consecutively():
     assert all(1 <= v <= READY_PERIOD < 2 ** 31 for v in vals)
     for s in [1, READY_PERIOD - 1, READY_PERIOD, READY_PERIOD + 1, 5 * READY_PERIOD]:
         assert ready_value(s + 1) != ready_value(s)
+
+
+def test_traced_profiling_build_loads_on_request():
+    """``_lib.use_traced_build()`` before the first load selects the profiling variant of the library
+    (``libmkx_trace.so``), which exports the same entry points; after a load it refuses."""
+    from reki_megakernel_b200 import _lib
+    from reki_megakernel_b200 import build as B
+    if B.stale(B.TRACE_LIB):
+        try:
+            B.nvcc()
+        except RuntimeError:
+            pytest.skip("no traced build and no nvcc")
+    code = "from reki_megakernel_b200 import _lib; _lib.use_traced_build(); _lib.load(); print(_lib.lib_path().name)"
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, cwd=ROOT, timeout=600)
+    assert r.returncode == 0, r.stderr
+    assert r.stdout.split()[0] == "libmkx_trace.so"
+    nm = shutil.which("nm")
+    if nm:
+        out = subprocess.run([nm, "-D", "--defined-only", str(B.TRACE_LIB)], capture_output=True, text=True).stdout
+        assert set(declared_symbols()) <= set(re.findall(r"\b(mkx_[a-z0-9_]+)\b", out))
+    _lib.load()
+    with pytest.raises(RuntimeError):
+        _lib.use_traced_build()
