@@ -46,7 +46,7 @@ constexpr int NT = 256, NW = 8;          // threads / warps per CTA
 constexpr int ISSUER = NT - 1;           // thread that refills weight / modulation slots
 constexpr int TP = 16;                   // padded action rows
 constexpr int AO = 8;                    // carried action dims (src/mk_expert.py:478)
-constexpr int XS = H + 8;                // shared X row stride (bf16 elements): conflict-free B loads
+constexpr int XS = H + 16;               // shared X row stride (bf16 elements): conflict-free 8-byte B loads
 constexpr int HWORDS = H / 2;            // exchange words per H-wide row
 constexpr int QKVWORDS = 3 * H / 2;
 constexpr int XWORDS = 32;               // exchange words per action-state row (fp32 payloads)
@@ -139,7 +139,10 @@ struct Cta {
 };
 // Shared-memory regions (offsets live in the kernel parameters, so nothing stays in registers).
 __device__ __forceinline__ char* cSlot(const Params& p, const Cta& c, int s) { return g_smem + p.s_slot[s]; }
-__device__ __forceinline__ char* cX(const Params& p, const Cta& c) { return g_smem + p.s_x; }       // [TP][XS] bf16
+// X: [TP][XS] bf16, each 16-column block stored as columns 0,1,8,9, 2,3,10,11, ..., 6,7,14,15 (the
+// mma.sync B-fragment order): the four columns of exchange word pair q sit at bytes [8q, 8q + 8) of
+// a row, and a lane's B fragment of a k-block is one 8-byte load.
+__device__ __forceinline__ char* cX(const Params& p, const Cta& c) { return g_smem + p.s_x; }
 __device__ __forceinline__ float* cP(const Params& p, const Cta& c) {                          // partials / attention
   return reinterpret_cast<float*>(g_smem + p.s_p);
 }
@@ -371,9 +374,9 @@ __device__ int stage_rows_adarms(const Params& p, Cta& c, const u64* rows, uint3
   } else {
 #pragma unroll
     for (int j = 0; j < SPAIRS; ++j) {
-      const int ca = col_a_of(part + SROW * j);
-      w0[j] = *reinterpret_cast<const uint32_t*>(xrow + ca * 2);
-      w1[j] = *reinterpret_cast<const uint32_t*>(xrow + (ca + 8) * 2);
+      const uint2 v = *reinterpret_cast<const uint2*>(xrow + (size_t)(part + SROW * j) * 8);
+      w0[j] = v.x;
+      w1[j] = v.y;
     }
   }
   // Sum of squares in four independent chains (12 FMAs deep instead of 48), then across the row's
@@ -417,9 +420,11 @@ __device__ int stage_rows_adarms(const Params& p, Cta& c, const u64* rows, uint3
   }
   if (rows != nullptr) MKX_TRACE_AFTER(1, outv[2 * SPAIRS - 1] ^ outv[0]);
 #pragma unroll
+  for (int i = 0; i < SPAIRS; ++i)  // word pair q of the row = X bytes [8q, 8q + 8)
+    *reinterpret_cast<uint2*>(xrow + (size_t)(part + SROW * i) * 8) = make_uint2(outv[2 * i], outv[2 * i + 1]);
+#pragma unroll
   for (int j = 0; j < 2 * SPAIRS; ++j) {
     const int col = col_a_of(part + SROW * (j >> 1)) + 8 * (j & 1);
-    *reinterpret_cast<uint32_t*>(xrow + col * 2) = outv[j];
     // c0 and R_h are even: a column pair is entirely inside or outside the residual columns
     if (live && (unsigned)(col - c.c0) < (unsigned)c.R_h) {
       const uint32_t u = payload_of((j & 1) ? w1[j >> 1] : w0[j >> 1]);
@@ -476,18 +481,18 @@ __device__ void mma_from_x(const Params& p, Cta& c, const char* wslot, int nmat,
     const int kb0 = (ksl * KB) >> q.lks, kb1 = ((ksl + 1) * KB) >> q.lks;
     const int ra = mm * 16 + g, rb = ra + 8;
     const bool va = ra < R, vb = rb < R;
-    const char* x0 = cX(p, c) + (size_t)g * XS * 2 + cc * 4;
-    const char* x1 = cX(p, c) + (size_t)(8 + g) * XS * 2 + cc * 4;
+    const char* x0 = cX(p, c) + (size_t)g * XS * 2 + cc * 8;
+    const char* x1 = cX(p, c) + (size_t)(8 + g) * XS * 2 + cc * 8;
 #pragma unroll 4
     for (int kb = kb0; kb < kb1; ++kb) {
       const char* blk = A + (size_t)kb * R * 32;
       const uint2 a = va ? lds64(blk + ra * 32) : make_uint2(0u, 0u);
       const uint2 b = vb ? lds64(blk + rb * 32) : make_uint2(0u, 0u);
-      const uint32_t b0 = lds32(x0 + kb * 32), b1 = lds32(x0 + kb * 32 + 16);
-      mma_bf16(d0, a.x, b.x, a.y, b.y, b0, b1);
+      const uint2 bx = lds64(x0 + kb * 32);
+      mma_bf16(d0, a.x, b.x, a.y, b.y, bx.x, bx.y);
       if (two) {
-        const uint32_t e0 = lds32(x1 + kb * 32), e1 = lds32(x1 + kb * 32 + 16);
-        mma_bf16(d1, a.x, b.x, a.y, b.y, e0, e1);
+        const uint2 ex = lds64(x1 + kb * 32);
+        mma_bf16(d1, a.x, b.x, a.y, b.y, ex.x, ex.y);
       }
     }
   }
@@ -1017,8 +1022,8 @@ __device__ int take_new_x(const Params& p, Cta& c, const u64* xrows, uint32_t xt
 }
 
 // In-projection h0 = bf16(xpad[:AO] @ Win[:AO] + bin) in fp32 (src/mk_expert.py:280-293) into X
-// (natural layout); thread t owns columns t, t + NT, ... below H, whose Win / bin values it loads
-// up front.
+// (in X's permuted column order); thread t owns columns t, t + NT, ... below H, whose Win / bin
+// values it loads up front.
 __device__ __forceinline__ void load_inproj(const Params& p, const Cta& c, float (&win)[NCOL][AO], float (&bin)[NCOL]) {
 #pragma unroll
   for (int k = 0; k < NCOL; ++k) {
@@ -1041,7 +1046,9 @@ __device__ void in_proj_to_x(const Params& p, Cta& c, const float (&win)[NCOL][A
       float acc = bin[k];
 #pragma unroll
       for (int a = 0; a < AO; ++a) acc = fmaf(xp[a], win[k][a], acc);
-      reinterpret_cast<__nv_bfloat16*>(cX(p, c))[(size_t)n * XS + c.tid + NT * k] =
+      const int col = c.tid + NT * k;  // X holds each 16-column block as 0,1,8,9, 2,3,10,11, ...
+      const int pos = (col & ~15) + ((col & 7) >> 1) * 4 + ((col >> 3) & 1) * 2 + (col & 1);
+      reinterpret_cast<__nv_bfloat16*>(cX(p, c))[(size_t)n * XS + pos] =
           __float2bfloat16_rn(n < p.T ? acc : 0.f);
     }
   }
