@@ -42,7 +42,7 @@ L2_FLUSH_BYTES = 256 << 20
 
 def algorithmic_bytes_per_step(dims, mods_row_bytes: int) -> int:
     """HBM bytes one Euler step must stream: bf16 weights + fp32 in/out projections + norm weights +
-    one modulation row (BASELINE.md roofline figures)."""
+    one modulation row, 212,678,400 B at the BASELINE configs[1] shapes (bf16 modulation row)."""
     L, H, I, A, HD = dims.L, dims.H, dims.I, dims.A, dims.HD
     bf16 = 2 * L * (3 * H * H + 3 * H * H + 3 * H * I)
     fp32 = 4 * (2 * A * H)

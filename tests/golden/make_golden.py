@@ -1,6 +1,8 @@
 """Generate golden fixtures by running the REFERENCE megakernel on identical seeded inputs.
 
-    python tests/golden/make_golden.py [--ref /root/reference] [--configs small full]
+    python tests/golden/make_golden.py --ref <reference checkout> [--configs small full]
+
+(``--ref`` defaults to the ``REKI_REFERENCE`` environment variable.)
 
 The reference's Triton kernel (``src/mk_expert.py``, class ``ExpertMegakernel`` and kernel
 ``expert_megakernel``) is imported unmodified from the reference checkout and executed on the CPU
@@ -203,9 +205,12 @@ def run_reference(ref_src: Path, cfg: dict):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("REKI_REFERENCE"),
+                    help="root of the reference checkout (the directory holding src/mk_expert.py)")
     ap.add_argument("--configs", nargs="*", default=list(CONFIGS))
     a = ap.parse_args()
+    if not a.ref:
+        ap.error("--ref (or REKI_REFERENCE) must name the reference checkout")
     out_dir = Path(__file__).resolve().parent
     for name in a.configs:
         cfg = CONFIGS[name]
