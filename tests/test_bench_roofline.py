@@ -1,0 +1,28 @@
+"""CPU checks of the roofline figures ``bench.py`` reports: the algorithmic bytes one Euler step must
+stream from HBM at the BASELINE configs[1] shapes, and the ncu traffic figure read from the committed
+expert-kernel profile summary."""
+import sys
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[1]
+sys.path.insert(0, str(ROOT))
+
+import bench  # noqa: E402
+from reki_megakernel_b200.synthetic import ExpertDims  # noqa: E402
+
+
+def test_algorithmic_bytes_per_euler_step():
+    d = ExpertDims()
+    mods_row = 2 * d.MODW                       # one bf16 modulation row: 70,656 values
+    assert mods_row == 141_312
+    per_step = bench.algorithmic_bytes_per_step(d, mods_row)
+    # bf16 weights 212,336,640 + fp32 in/out projections 196,608 + norm weights 3,840 + one row
+    assert per_step == 212_336_640 + 196_608 + 3_840 + 141_312 == 212_678_400
+    assert 9 * per_step == 1_914_105_600        # one launch = Euler steps 2..10
+
+
+def test_traffic_figure_is_read_from_the_profile_summary():
+    t = bench.traffic_from_profile()
+    assert t is not None
+    # ncu's DRAM bytes of one launch: within 1 % of the algorithmic bytes (no re-reads)
+    assert abs(t / 1_914_105_600 - 1.0) < 0.01
