@@ -1623,7 +1623,8 @@ extern "C" mkx_status mkx_create(const mkx_dims* dims, const mkx_weights* w, int
                         w->win, w->bin, w->wout, w->bout};
   for (const void* q : ptrs)
     if (!q) return MKX_ERR_INVALID_ARG;
-  MKX_CUDA(cudaSetDevice(device));
+  DeviceScope dev_scope(device);
+  MKX_CUDA(dev_scope.err);
   int sms = 0, smem_optin = 0;
   MKX_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
   MKX_CUDA(cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
@@ -1805,7 +1806,8 @@ extern "C" int mkx_sync_points(const mkx_handle* h, int n_steps) {
 extern "C" mkx_status mkx_last_error(mkx_handle* h, int* code, long long* stages) {
   if (!h) return MKX_ERR_INVALID_ARG;
   int st[4] = {0, 0, 0, 0};
-  MKX_CUDA(cudaSetDevice(h->device));
+  DeviceScope dev_scope(h->device);
+  MKX_CUDA(dev_scope.err);
   MKX_CUDA(cudaMemcpy(st, h->base.status, sizeof(st), cudaMemcpyDeviceToHost));
   if (code) *code = st[0];
   if (stages) {
@@ -1818,7 +1820,8 @@ extern "C" mkx_status mkx_last_error(mkx_handle* h, int* code, long long* stages
 
 extern "C" mkx_status mkx_clear_error(mkx_handle* h) {
   if (!h) return MKX_ERR_INVALID_ARG;
-  MKX_CUDA(cudaSetDevice(h->device));
+  DeviceScope dev_scope(h->device);
+  MKX_CUDA(dev_scope.err);
   int st[4] = {0, 0, 0, 0};
   MKX_CUDA(cudaMemcpy(st, h->base.status, sizeof(st), cudaMemcpyDeviceToHost));
   st[0] = 0;
@@ -1849,7 +1852,7 @@ extern "C" mkx_status mkx_launch_shape(const mkx_handle* h, int* grid, int* smem
 
 extern "C" void mkx_destroy(mkx_handle* h) {
   if (!h) return;
-  cudaSetDevice(h->device);
+  DeviceScope dev_scope(h->device);
   for (int i = 0; i < h->nalloc; ++i) cudaFree(h->alloc[i]);
   delete h;
 }

@@ -241,7 +241,8 @@ extern "C" int mkx_mods_width(const mkx_mods_handle* h) { return h ? h->MODW : 0
 
 extern "C" mkx_status mkx_mods_input(mkx_mods_handle* h, uint16_t* dst, cudaStream_t stream) {
   if (!h || !dst) return MKX_ERR_INVALID_ARG;
-  if (cudaSetDevice(h->device) != cudaSuccess ||
+  mkx::DeviceScope dev_scope(h->device);
+  if (dev_scope.err != cudaSuccess ||
       cudaMemcpyAsync(dst, h->act, (size_t)NMAX * H * 2, cudaMemcpyDeviceToDevice, stream) != cudaSuccess)
     return MKX_ERR_CUDA;
   return MKX_OK;
@@ -255,7 +256,8 @@ extern "C" mkx_status mkx_mods_create(const mkx_mods_dims* dims, const float* w_
   if (d.H != H || d.L < 1 || d.L > 64 || d.tdim < 64 || d.tdim > TDIM_MAX || d.tdim % 64 != 0 || d.sdim < 1 ||
       d.sdim > SDIM_MAX)
     return MKX_ERR_UNSUPPORTED;
-  if (cudaSetDevice(device) != cudaSuccess) return MKX_ERR_CUDA;
+  mkx::DeviceScope dev_scope(device);
+  if (dev_scope.err != cudaSuccess) return MKX_ERR_CUDA;
   int sms = 0;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return MKX_ERR_CUDA;
   mkx_mods_handle* h = new (std::nothrow) mkx_mods_handle();
@@ -294,7 +296,8 @@ extern "C" mkx_status mkx_mods_run(mkx_mods_handle* h, int N, const float* state
   if (!h || !state || !mods_out || !dt_out) return MKX_ERR_INVALID_ARG;
   if (N < 1 || N > NMAX) return MKX_ERR_INVALID_ARG;
   if ((reinterpret_cast<uintptr_t>(mods_out) & 3) != 0) return MKX_ERR_INVALID_ARG;
-  if (cudaSetDevice(h->device) != cudaSuccess) return MKX_ERR_CUDA;
+  mkx::DeviceScope dev_scope(h->device);
+  if (dev_scope.err != cudaSuccess) return MKX_ERR_CUDA;
   cond_kernel<<<H / CW, CT, (size_t)N * h->d.tdim * 4, stream>>>(h->w_t, h->w_s, state, h->temb, N, h->d.tdim, h->d.sdim, h->act, dt_out);
   if (cudaGetLastError() != cudaSuccess) return MKX_ERR_CUDA;
   // programmatic dependent launch: the projection may start while the conditioning runs
@@ -318,7 +321,8 @@ extern "C" mkx_status mkx_mods_run(mkx_mods_handle* h, int N, const float* state
 
 extern "C" mkx_status mkx_mods_last_error(mkx_mods_handle* h, int* code) {
   if (!h || !code) return MKX_ERR_INVALID_ARG;
-  if (cudaSetDevice(h->device) != cudaSuccess || cudaStreamSynchronize(h->last_stream) != cudaSuccess ||
+  mkx::DeviceScope dev_scope(h->device);
+  if (dev_scope.err != cudaSuccess || cudaStreamSynchronize(h->last_stream) != cudaSuccess ||
       cudaMemcpy(code, h->status, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
     return MKX_ERR_CUDA;
   return MKX_OK;
@@ -326,7 +330,7 @@ extern "C" mkx_status mkx_mods_last_error(mkx_mods_handle* h, int* code) {
 
 extern "C" void mkx_mods_destroy(mkx_mods_handle* h) {
   if (!h) return;
-  cudaSetDevice(h->device);
+  mkx::DeviceScope dev_scope(h->device);
   if (h->w_t) cudaFree(h->w_t);
   if (h->w_s) cudaFree(h->w_s);
   if (h->wpk) cudaFree(h->wpk);

@@ -302,7 +302,8 @@ extern "C" mkx_status mkx_prep_create(const mkx_prep_dims* dims, const uint16_t*
   if (d.H != H || d.NH != NH || d.HD != HD || d.L < 1 || d.L > 64 || d.src_dim < BK || d.src_dim % BK != 0)
     return MKX_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(wkv) & 15) != 0) return MKX_ERR_INVALID_ARG;
-  if (cudaSetDevice(device) != cudaSuccess) return MKX_ERR_CUDA;
+  mkx::DeviceScope dev_scope(device);
+  if (dev_scope.err != cudaSuccess) return MKX_ERR_CUDA;
   mkx_prep_handle* h = new (std::nothrow) mkx_prep_handle();
   if (!h) return MKX_ERR_RESOURCES;
   memset(h, 0, sizeof(*h));
@@ -337,7 +338,8 @@ extern "C" mkx_status mkx_prep_run(mkx_prep_handle* h, const uint16_t* src, int 
   if ((reinterpret_cast<uintptr_t>(src) & 15) != 0 || (reinterpret_cast<uintptr_t>(k_out) & 15) != 0 ||
       (reinterpret_cast<uintptr_t>(v_out) & 15) != 0)
     return MKX_ERR_INVALID_ARG;
-  if (cudaSetDevice(h->device) != cudaSuccess) return MKX_ERR_CUDA;
+  mkx::DeviceScope dev_scope(h->device);
+  if (dev_scope.err != cudaSuccess) return MKX_ERR_CUDA;
   const int ntok = S >= MAXN ? MAXN : ((S + 15) / 16) * 16;
   CUtensorMap ts;
   if (!encode_bf16(&ts, src, (uint64_t)S, (uint64_t)h->d.src_dim, (uint32_t)ntok)) return MKX_ERR_CUDA;
@@ -375,7 +377,8 @@ extern "C" mkx_status mkx_prep_run(mkx_prep_handle* h, const uint16_t* src, int 
 
 extern "C" mkx_status mkx_prep_last_error(mkx_prep_handle* h, int* code) {
   if (!h || !code) return MKX_ERR_INVALID_ARG;
-  if (cudaSetDevice(h->device) != cudaSuccess || cudaStreamSynchronize(h->last_stream) != cudaSuccess ||
+  mkx::DeviceScope dev_scope(h->device);
+  if (dev_scope.err != cudaSuccess || cudaStreamSynchronize(h->last_stream) != cudaSuccess ||
       cudaMemcpy(code, h->status, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
     return MKX_ERR_CUDA;
   return MKX_OK;
@@ -383,7 +386,7 @@ extern "C" mkx_status mkx_prep_last_error(mkx_prep_handle* h, int* code) {
 
 extern "C" void mkx_prep_destroy(mkx_prep_handle* h) {
   if (!h) return;
-  cudaSetDevice(h->device);
+  mkx::DeviceScope dev_scope(h->device);
   if (h->wpk) cudaFree(h->wpk);
   if (h->kn) cudaFree(h->kn);
   if (h->status) cudaFree(h->status);
