@@ -3,7 +3,10 @@
  *
  * Plain C: device pointers, sizes and a cudaStream_t; no torch types. Every entry point returns an
  * mkx_status (0 = success). All pointers marked "device" must point to memory of the device the
- * handle was created on.
+ * handle was created on. Entry points that need the handle's device (create, error read-back,
+ * clear, destroy) make it current for the call and restore the caller's current device before
+ * they return; mkx_run and mkx_run_static launch on the device of the stream they are given, which
+ * must be the calling thread's current device.
  *
  * Reference interface each entry point replaces (project muninn-huginn/reki-megakernel):
  *   mkx_create      <- ExpertMegakernel.__init__(model)            src/mk_expert.py:436-481

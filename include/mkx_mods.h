@@ -19,7 +19,10 @@
  * HBM once per call for all N steps (tensor-core mma.sync tiles of 16 rows x 16 steps).
  *
  * All pointers are device pointers of the handle's device unless marked otherwise; bf16 arrays
- * are uint16_t bit patterns. Status codes are those of mkx.h. */
+ * are uint16_t bit patterns. Status codes are those of mkx.h. *
+ * Entry points that select the handle's device make it current for the call and restore the
+ * caller's current device before they return.
+ */
 #ifndef MKX_MODS_H
 #define MKX_MODS_H
 

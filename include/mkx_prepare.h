@@ -14,7 +14,10 @@
  * This entry point has no counterpart in the reference megakernel itself.
  *
  * All pointers are device pointers of the handle's device unless marked otherwise; bf16 arrays
- * are uint16_t bit patterns. Status codes are those of mkx.h. */
+ * are uint16_t bit patterns. Status codes are those of mkx.h. *
+ * Entry points that select the handle's device make it current for the call and restore the
+ * caller's current device before they return.
+ */
 #ifndef MKX_PREPARE_H
 #define MKX_PREPARE_H
 
