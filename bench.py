@@ -104,79 +104,96 @@ class Clocks:
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
+KERNEL_SOURCES = ("reki_megakernel_b200/csrc/mk_expert.cu", "reki_megakernel_b200/csrc/mkx_device.cuh")
+
+
+def kernel_source_sha() -> str:
+    """sha256 (first 16 hex digits) of the expert kernel's sources, as recorded in the ncu summary."""
+    import hashlib
+    h = hashlib.sha256()
+    for f in KERNEL_SOURCES:
+        h.update((ROOT / f).read_bytes())
+    return h.hexdigest()[:16]
+
+
 def traffic_from_profile():
-    """dram bytes (read + write) per launch of expert_kernel, from the committed ncu summary."""
+    """(dram bytes read + written per launch of expert_kernel, source note) from the committed ncu
+    summary, or (None, why) when the summary was captured from other kernel sources than these."""
     p = ROOT / "profiles" / "expert_kernel_full.md"
     if not p.exists():
-        return None
+        return None, "no ncu summary"
+    traffic, sha = None, None
     for line in p.read_text().splitlines():
         if line.startswith("traffic_bytes_per_launch:"):
             try:
-                return int(line.split(":", 1)[1].strip().split()[0])
+                traffic = int(line.split(":", 1)[1].strip().split()[0])
             except ValueError:
-                return None
-    return None
+                traffic = None
+        if line.startswith("kernel_source_sha16:"):
+            sha = line.split(":", 1)[1].strip().split()[0]
+    if sha != kernel_source_sha():
+        return None, f"ncu summary captured from other kernel sources ({sha}), not these ({kernel_source_sha()})"
+    return traffic, f"ncu capture of these kernel sources (sha {sha}), profiles/expert_kernel_full.md"
 
 
 # ------------------------------------------------------------------------------------------------
-def cpu_oracle_time(dims, seconds: float, threads: int):
-    """fp32 eager CPU expert (the oracle), one Euler step at a time on this host's cores; returns
-    (ms per predict = 9 Euler steps, Euler steps run, threads)."""
+def cpu_predict_ms(dims, S: int, threads: int, warmup: int, min_n: int, seconds: float):
+    """fp32 eager CPU expert (the oracle), whole predicts (Euler steps 2..10 of one episode) on this
+    host's cores; returns the per-predict times in ms (at least min_n, or until `seconds` elapsed)."""
     from oracle.expert_oracle import OracleExpert
     from reki_megakernel_b200.synthetic import make_inputs, make_weights
     torch.set_num_threads(threads)
-    w = make_weights(dims, seed=0)
-    orc = OracleExpert(w, "fp32")
-    inp = make_inputs(dims, n_steps=1)
+    orc = OracleExpert(make_weights(dims, seed=0), "fp32")
+    inp = make_inputs(dims, n_steps=9, S=S)
     e = inp.episode(0)
     ep = dict(x=e.x[0], mods=e.mods[0], dt=e.dt[0], memk=e.memk[0], memv=e.memv[0], kv_start=int(e.kv_start[0]),
               kca=e.kca[0], vca=e.vca[0], S=int(e.S[0]), sa_cos=e.sa_cos[0], sa_sin=e.sa_sin[0],
               ca_cos=e.ca_cos[0], ca_sin=e.ca_sin[0], action_dim=inp.action_dim)
-    orc.run_episode(ep)  # warm-up
-    n, t0 = 0, time.perf_counter()
-    times = []
-    while time.perf_counter() - t0 < seconds or n < 3:
+    for _ in range(warmup):
+        orc.run_episode(ep)
+    times, t0 = [], time.perf_counter()
+    while len(times) < min_n or (seconds > 0 and time.perf_counter() - t0 < seconds):
         a = time.perf_counter()
         orc.run_episode(ep)
-        times.append(time.perf_counter() - a)
-        n += 1
-    return 9 * statistics.median(times) * 1e3, n, threads
+        times.append((time.perf_counter() - a) * 1e3)
+    return times
+
+
+def bench_config(args, world: int) -> dict:
+    """The workload description shared by both arms (the reference arm runs the same workload on the
+    host cores)."""
+    return {"workload": "REKI expert Euler steps 2-10 (BASELINE configs[1]); one step = one predict of each "
+                        "of this GPU's episodes, batch-1 launches back to back",
+            "T": 10, "S": args.S, "memory_rows": 64, "euler_steps": 9, "episodes_per_gpu": args.batch,
+            "parallelism": f"replicas x{world}, no collective",
+            "l2": "256 MB written between timed steps (untimed); weights (212 MB/Euler step) exceed L2",
+            "timing": "CUDA-graph replay, CUDA events per step, mean over steps, max over ranks"}
 
 
 def run_reference(args, rank: int, world: int):
+    """The reference algorithm's CPU implementation (the fp32 oracle: Kyutai's eager expert is not
+    available here) on all host cores, rank 0 only: `--warmup` untimed then `--steps` timed whole
+    predicts (capped at --max-ref-steps), median per predict."""
     if rank != 0:
         return
     from reki_megakernel_b200.synthetic import ExpertDims
     dims = ExpertDims()
     threads = len(os.sched_getaffinity(0))
-    # --warmup / --steps count Euler steps of the CPU expert here (each ~0.1-1 s); a predict is 9.
-    from oracle.expert_oracle import OracleExpert
-    from reki_megakernel_b200.synthetic import make_inputs, make_weights
-    torch.set_num_threads(threads)
-    orc = OracleExpert(make_weights(dims, seed=0), "fp32")
-    inp = make_inputs(dims, n_steps=1, S=args.S)
-    e = inp.episode(0)
-    ep = dict(x=e.x[0], mods=e.mods[0], dt=e.dt[0], memk=e.memk[0], memv=e.memv[0], kv_start=int(e.kv_start[0]),
-              kca=e.kca[0], vca=e.vca[0], S=int(e.S[0]), sa_cos=e.sa_cos[0], sa_sin=e.sa_sin[0],
-              ca_cos=e.ca_cos[0], ca_sin=e.ca_sin[0], action_dim=inp.action_dim)
-    for _ in range(args.warmup):
-        orc.run_episode(ep)
     steps = min(args.steps, args.max_ref_steps)
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        orc.run_episode(ep)
-    el = time.perf_counter() - t0
-    ms_predict = 9 * el / steps * 1e3
+    times = cpu_predict_ms(dims, args.S, threads, args.warmup, steps, 0.0)
+    ms_predict = statistics.median(times)
     value = 1000.0 / ms_predict
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "episodes/s", "n_gpus": args.gpus,
-        "steps": steps, "warmup": args.warmup, "ms_per_step": ms_predict, "ms_per_predict": ms_predict,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "REKI expert steps 2-10, batch 1 (BASELINE configs[1] shapes), CPU fp32 eager",
-                   "T": 10, "S": args.S, "memory_rows": 64, "euler_steps": 9},
+        "steps": len(times), "warmup": args.warmup, "ms_per_step": ms_predict, "ms_per_predict": ms_predict,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded weights, BASELINE configs[1] shapes)",
+        "config": bench_config(args, world),
         "cpu_baseline": {"value": value, "unit": "episodes/s", "cores": threads, "kind": "port",
-                         "sample": f"{steps} Euler steps of one episode (x9 = ms per predict), fp32 oracle"},
+                         "sample": f"{len(times)} whole predicts (9 Euler steps each) of one episode, fp32 CPU oracle, "
+                                   "median"},
         "e2e": {"value": value, "unit": "episodes/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "wall_s_timed_region": sum(times) / 1e3,
     }
     print(json.dumps(line), flush=True)
 
@@ -637,6 +654,7 @@ def run_mk(args, rank: int, world: int):
     hbm, peak_kind = peaks()
     mods_row = dims.MODW * 2
     bytes_step = algorithmic_bytes_per_step(dims, mods_row)
+    traffic, traffic_src = traffic_from_profile()
     # one launch streams the weights once: per-launch bytes over per-launch time
     achieved = 9 * bytes_step / (ms / args.batch * 1e-3) / 1e9
     line = {
@@ -646,17 +664,12 @@ def run_mk(args, rank: int, world: int):
         "ms_per_step_p50": statistics.median(per), "ms_per_step_p99": sorted(per)[min(len(per) - 1, int(0.99 * len(per)))],
         "higher_is_better": True, "scaling": "weak",
         "vs_baseline": job_episodes_per_s(world, args.batch, ms_max) / (1000.0 / PUBLISHED_MS),
-        "dtype": "bf16", "data": "synthetic (seeded N(0,0.02) weights, BASELINE configs[1] shapes)",
-        "config": {"workload": "REKI expert Euler steps 2-10 (BASELINE configs[1]); one step = one predict of each "
-                               "of this GPU's episodes, batch-1 launches back to back",
-                   "T": 10, "S": args.S, "memory_rows": 64, "euler_steps": 9, "episodes_per_gpu": args.batch,
-                   "parallelism": f"replicas x{world}, no collective",
-                   "l2": "256 MB written between timed steps (untimed); weights (212 MB/Euler step) exceed L2",
-                   "timing": "CUDA-graph replay, CUDA events per step, mean over steps, max over ranks"},
+        "dtype": "bf16", "data": "synthetic (seeded weights, BASELINE configs[1] shapes)",
+        "config": bench_config(args, world),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "peak_kind": f"{peak_kind} (hbm copy, burst)",
-                     "traffic": traffic_from_profile() if args.S == 160 else None,
-                     "algorithmic_bytes_per_launch": 9 * bytes_step},
+                     "traffic": traffic if args.S == 160 and args.batch == 1 else None,
+                     "traffic_source": traffic_src, "algorithmic_bytes_per_launch": 9 * bytes_step},
         "e2e": {"value": job_episodes_per_s(world, args.batch, e2e_max), "unit": "episodes/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_max},
         "gpu_launches": args.steps * args.batch,
@@ -664,10 +677,12 @@ def run_mk(args, rank: int, world: int):
         "wall_s_timed_region": wall,
     }
     if world == 1 and not args.no_cpu_baseline:
-        cpu_ms, n, thr = cpu_oracle_time(dims, args.cpu_seconds, len(os.sched_getaffinity(0)))
+        thr = len(os.sched_getaffinity(0))
+        times = cpu_predict_ms(dims, args.S, thr, 1, 3, args.cpu_seconds)
+        cpu_ms = statistics.median(times)
         line["cpu_baseline"] = {"value": 1000.0 / cpu_ms, "unit": "episodes/s", "cores": thr, "kind": "port",
-                                "sample": f"{n} Euler steps of one episode, fp32 CPU oracle; x9 per predict",
-                                "ms_per_predict": cpu_ms}
+                                "sample": f"{len(times)} whole predicts (9 Euler steps each) of one episode, fp32 CPU "
+                                          "oracle, median", "ms_per_predict": cpu_ms}
     print(json.dumps(line), flush=True)
 
 

@@ -18,8 +18,8 @@
  *                      (error word) the reference has none: a broken grid barrier deadlocks
  *                      (README.md:262-263); here every device-side wait is bounded and reports
  *   mkx_destroy     <- Python object lifetime of ExpertMegakernel
- *   mkx_set_timeout_ns, mkx_clear_error, mkx_set_fault_injection, mkx_launch_shape,
- *   mkx_last_cuda_error <- no counterpart (bounded waits, their test hook, introspection)
+ *   mkx_set_timeout_ns, mkx_clear_error, mkx_set_fault_injection, mkx_set_launch_sequence,
+ *   mkx_launch_shape, mkx_last_cuda_error <- no counterpart (bounded waits, test hooks, introspection)
  */
 #ifndef MKX_H_
 #define MKX_H_
@@ -144,6 +144,13 @@ mkx_status mkx_set_timeout_ns(mkx_handle* h, unsigned long long ns);
  * MKX_ERR_DEVICE through mkx_last_error. 0 disables it. */
 mkx_status mkx_set_fault_injection(mkx_handle* h, int stage);
 
+/* Test hook: sets the handle's launch sequence number (synchronous). Exchange-word tags are
+ * sequence * 4096 + instance + 1 in 32 bits, so they repeat every 2^20 launches; every launch sets
+ * the words it will not rewrite (rows >= T, action-state words >= action_dim, an unused parity) to
+ * tag 0, so a launch exactly 2^20 launches later never finds a stale word with its own tag. The hook
+ * lets a test jump the sequence by 2^20 instead of running a million launches. */
+mkx_status mkx_set_launch_sequence(mkx_handle* h, unsigned int seq);
+
 /* Grid size actually used and dynamic shared memory bytes per CTA. */
 mkx_status mkx_launch_shape(const mkx_handle* h, int* grid, int* smem_bytes);
 
@@ -166,13 +173,16 @@ typedef struct {
  * can block on the device and break the loop's timing. It runs one launch of the same kernel as
  * mkx_run without a handle: the caller passes packed weights (mkx_packed_weights, packed for
  * dims->grid; 0 = one CTA per SM), the step inputs and x_out, all in memory it owns, plus an
- * optional device int err_out that receives the launch's error word (0 when every wait finished).
+ * optional device int err_out (4-byte aligned, else MKX_ERR_INVALID_ARG) that receives the launch's
+ * error word (0 when every wait finished).
  * The kernel's scratch -- the exchange buffers and status words -- is a file-scope static device
  * array of 2,072,608 bytes, which every GPU that loads this library keeps until the process exits;
  * it holds I <= 3072 and T <= 16, and larger sizes return MKX_ERR_UNSUPPORTED with a message in
  * mkx_last_cuda_error(). Nothing in this call allocates. The first call on a device looks up the
  * array's device address and raises the kernel's shared-memory limit, so make that first call
- * before any stream capture. All calls share the one array and it keeps the last call's contents
+ * before any stream capture. That set-up is kept for the life of the process: after a
+ * cudaDeviceReset (or any reset of the device's primary context) the address and the limit are
+ * stale, so do not call this entry point on that device again in the same process. All calls share the one array and it keeps the last call's contents
  * (the error word and stage counter are cleared on the stream before each launch): two calls
  * whose launches overlap on the GPU race and corrupt each other. */
 mkx_status mkx_run_static(const mkx_dims* dims, const mkx_packed_weights* w, const mkx_step_inputs* in,

@@ -44,12 +44,13 @@ def _bf(t: torch.Tensor) -> torch.Tensor:
 class OracleExpert:
     """fp32 copies of the weights plus the per-step math; ``run`` integrates steps 2..N."""
 
-    def __init__(self, w: ExpertWeights, mode: str = "bf16"):
+    def __init__(self, w: ExpertWeights, mode: str = "bf16", device="cpu"):
         if mode not in ("bf16", "fp32"):
             raise ValueError(mode)
         self.mode = mode
         self.d = w.dims
-        f = lambda t: t.detach().to("cpu", torch.float32).contiguous()  # noqa: E731
+        self.dev = torch.device(device)
+        f = lambda t: t.detach().to(self.dev, torch.float32).contiguous()  # noqa: E731
         self.wqkv, self.wo, self.wqca, self.woca = f(w.wqkv), f(w.wo), f(w.wqca), f(w.woca)
         self.wg, self.wu, self.wd = f(w.wg), f(w.wu), f(w.wd)
         self.qn, self.kn, self.qcan = f(w.qn), f(w.kn), f(w.qcan)
@@ -76,9 +77,9 @@ class OracleExpert:
         HD = x.shape[-1]
         r = torch.rsqrt(x.pow(2).sum(-1, keepdim=True) / HD + self.qk_eps)
         xn = self._r(x * r * (1.0 + w))
-        perm = (torch.arange(HD) + HD // 2) % HD
+        perm = (torch.arange(HD, device=x.device) + HD // 2) % HD
         xpn = self._r(x[..., perm] * r * (1.0 + w[perm]))
-        sign = torch.where(torch.arange(HD) < HD // 2, -1.0, 1.0)
+        sign = torch.where(torch.arange(HD, device=x.device) < HD // 2, -1.0, 1.0)
         return self._r(xn * cos + sign * xpn * sin)
 
     # ---- attention ---------------------------------------------------------------------------
@@ -89,7 +90,7 @@ class OracleExpert:
         H, NH, HD = d.H, d.NH, d.HD
         scale = HD ** -0.5
         T = qkv.shape[0]
-        y = torch.empty(T, H)
+        y = torch.empty(T, H, device=qkv.device)
         for h in range(NH):
             sl = slice(h * HD, (h + 1) * HD)
             q = self._norm_rope(qkv[:, sl], self.qn[l], cos, sin)
@@ -99,7 +100,7 @@ class OracleExpert:
             mv = memv[l, kv_start:, h].float()
             s1 = (q @ mk.T) * scale
             s2 = (q @ k.T) * scale
-            mx = torch.maximum(s1.amax(1, keepdim=True) if s1.shape[1] else torch.full((T, 1), -float("inf")),
+            mx = torch.maximum(s1.amax(1, keepdim=True) if s1.shape[1] else torch.full((T, 1), -float("inf"), device=q.device),
                                s2.amax(1, keepdim=True))
             p1 = torch.exp(s1 - mx)
             p2 = torch.exp(s2 - mx)
@@ -115,7 +116,7 @@ class OracleExpert:
         H, NH, HD = d.H, d.NH, d.HD
         scale = HD ** -0.5
         T = qca.shape[0]
-        y = torch.empty(T, H)
+        y = torch.empty(T, H, device=qca.device)
         for h in range(NH):
             sl = slice(h * HD, (h + 1) * HD)
             q = self._norm_rope(qca[:, sl], self.qcan[l], cos, sin)
@@ -126,9 +127,9 @@ class OracleExpert:
                 p = torch.softmax(s, dim=1)
                 y[:, sl] = p @ v_all
                 continue
-            mx = torch.full((T, 1), -float("inf"))
-            den = torch.zeros(T, 1)
-            acc = torch.zeros(T, HD)
+            mx = torch.full((T, 1), -float("inf"), device=q.device)
+            den = torch.zeros(T, 1, device=q.device)
+            acc = torch.zeros(T, HD, device=q.device)
             for s0 in range(0, S, CA_BLOCK):
                 k = k_all[s0:s0 + CA_BLOCK]
                 v = v_all[s0:s0 + CA_BLOCK]
@@ -188,7 +189,7 @@ class OracleExpert:
         T, A = x.shape
         mods = ep["mods"].float()
         dt = float(ep["dt"])
-        keep = (torch.arange(A) < adim)[None, :]
+        keep = (torch.arange(A, device=x.device) < adim)[None, :]
         h = self.in_proj(torch.where(keep, x, 0.0))
         n_steps = mods.shape[0] - 1
         for s in range(n_steps):
@@ -206,12 +207,104 @@ class OracleExpert:
         """All episodes of ``inp``; returns [B, T, A] fp32 (the state after step N)."""
         outs = []
         for b in range(inp.x.shape[0]):
-            e = inp.episode(b).to("cpu")
+            e = inp.episode(b).to(self.dev)
             ep = dict(x=e.x[0], mods=e.mods[0], dt=e.dt[0], memk=e.memk[0], memv=e.memv[0],
                       kv_start=int(e.kv_start[0]), kca=e.kca[0], vca=e.vca[0], S=int(e.S[0]),
                       sa_cos=e.sa_cos[0].float(), sa_sin=e.sa_sin[0].float(),
                       ca_cos=e.ca_cos[0].float(), ca_sin=e.ca_sin[0].float(), action_dim=inp.action_dim)
             outs.append(self.run_episode(ep, trace if b == 0 else None))
+        return torch.stack(outs)
+
+
+def _native_layer(h, m_sa, m_ca, m_mlp, wqkv, wo, wqca, woca, wg, wu, wd, qn, kn, qcan, memk, memv, kca, vca,
+                  sa_cos, sa_sin, ca_cos, ca_sin, eps: float, qk_eps: float):
+    """One expert layer on native bf16 tensors (see ``NativeBf16Expert``). h [T, H] bf16; m_* [3H]
+    fp32 (scale, shift, gate); weights bf16 [N, K]; qn / kn / qcan fp32 [HD] (offsets, scale 1 + w);
+    memk / memv [M, NH, HD] bf16 (valid rows only); kca / vca [S, NH, HD] bf16 (valid rows only);
+    cos / sin fp32 [T, HD]. Returns h after the layer, bf16."""
+    T, H = h.shape
+    NH, HD = memk.shape[1], memk.shape[2]
+    bf = torch.bfloat16
+
+    def adarms(x, sc, sh):
+        xf = x.float()
+        return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * (1.0 + sc) + sh).to(bf)
+
+    def norm_rope(x, w, cos, sin):
+        xf = x.float()
+        xn = (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + qk_eps) * (1.0 + w)).to(bf).float()
+        rot = torch.cat([-xn[..., HD // 2:], xn[..., :HD // 2]], -1)
+        return (xn * cos[:, None] + rot * sin[:, None]).to(bf)
+
+    def attend(q, k, v):  # q [T, NH, HD], k / v [N, NH, HD] -> [T, H]
+        o = torch.nn.functional.scaled_dot_product_attention(q.transpose(0, 1)[None], k.transpose(0, 1)[None],
+                                                             v.transpose(0, 1)[None])
+        return o[0].transpose(0, 1).reshape(T, H)
+
+    def gated(res, o, gate):
+        return (res.float() + o.float() * gate).to(bf)
+
+    qkv = adarms(h, m_sa[:H], m_sa[H:2 * H]) @ wqkv.T
+    q = norm_rope(qkv[:, :H].reshape(T, NH, HD), qn, sa_cos, sa_sin)
+    k = norm_rope(qkv[:, H:2 * H].reshape(T, NH, HD), kn, sa_cos, sa_sin)
+    v = qkv[:, 2 * H:].reshape(T, NH, HD)
+    y = attend(q, torch.cat([memk, k], 0), torch.cat([memv, v], 0))
+    h2 = gated(h, y @ wo.T, m_sa[2 * H:3 * H])
+    qc = norm_rope((adarms(h2, m_ca[:H], m_ca[H:2 * H]) @ wqca.T).reshape(T, NH, HD), qcan, ca_cos, ca_sin)
+    h3 = gated(h2, attend(qc, kca, vca) @ woca.T, m_ca[2 * H:3 * H])
+    a = adarms(h3, m_mlp[:H], m_mlp[H:2 * H])
+    g = (torch.nn.functional.silu((a @ wg.T).float()) * (a @ wu.T).float()).to(bf)
+    return gated(h3, g @ wd.T, m_mlp[2 * H:3 * H])
+
+
+class NativeBf16Expert:
+    """The expert written the way a PyTorch model runs it in bf16, an implementation independent of
+    the oracle's rounding model: bf16 Linear layers (library GEMMs with fp32 accumulation and bf16
+    output), AdaRMS and gated residuals in fp32 rounded to bf16, per-head RMSNorm + rotate-half RoPE,
+    attention through ``scaled_dot_product_attention`` on bf16 q / k / v, SiLU-gated MLP, and the
+    oracle's fp32 step tail (``src/mk_expert.py:254-299``). ``compile=True`` runs every layer through
+    ``torch.compile`` (Inductor): the stand-in for the reference's compiled expert, which
+    ``src/test_mk.py:36-40`` compares with its eager expert and the megakernel (Kyutai's model is not
+    available here). Test infrastructure; meant for a CUDA device."""
+
+    def __init__(self, w: ExpertWeights, device="cuda", compile: bool = False):
+        self.tail = OracleExpert(w, "bf16", device)
+        self.dev = torch.device(device)
+        bf = torch.bfloat16
+        g = lambda t: t.detach().to(self.dev, bf).contiguous()  # noqa: E731
+        self.w = dict(wqkv=g(w.wqkv), wo=g(w.wo), wqca=g(w.wqca), woca=g(w.woca), wg=g(w.wg), wu=g(w.wu), wd=g(w.wd))
+        f = lambda t: t.detach().to(self.dev, torch.float32).contiguous()  # noqa: E731
+        self.qn, self.kn, self.qcan = f(w.qn), f(w.kn), f(w.qcan)
+        self.d = w.dims
+        self.eps, self.qk_eps = float(w.eps), float(w.qk_eps)
+        self.fn = torch.compile(_native_layer, dynamic=False) if compile else _native_layer
+
+    def run(self, inp: StepInputs) -> torch.Tensor:
+        d = self.d
+        L, H = d.L, d.H
+        outs = []
+        for b in range(inp.x.shape[0]):
+            e = inp.episode(b).to(self.dev)
+            adim = inp.action_dim
+            x = e.x[0].float().clone()
+            mods = e.mods[0].float()
+            dt = float(e.dt[0])
+            ks, S = int(e.kv_start[0]), int(e.S[0])
+            keep = (torch.arange(x.shape[1], device=self.dev) < adim)[None, :]
+            h = self.tail.in_proj(torch.where(keep, x, 0.0)).to(torch.bfloat16)
+            for s in range(mods.shape[0] - 1):
+                mrow = mods[1 + s]
+                for l in range(L):
+                    m = mrow[9 * H * l:]
+                    h = self.fn(h, m[:3 * H], m[3 * H:6 * H], m[6 * H:9 * H],
+                                *(self.w[k][l] for k in ("wqkv", "wo", "wqca", "woca", "wg", "wu", "wd")),
+                                self.qn[l], self.kn[l], self.qcan[l], e.memk[0, l, ks:], e.memv[0, l, ks:],
+                                e.kca[0, l, :S], e.vca[0, l, :S], e.sa_cos[0].float(), e.sa_sin[0].float(),
+                                e.ca_cos[0].float(), e.ca_sin[0].float(), self.eps, self.qk_eps)
+                v = self.tail.velocity(h.float(), mrow[9 * H * L:])
+                x = torch.where(keep, x, 0.0) + dt * v
+                h = self.tail.in_proj(torch.where(keep, x, 0.0)).to(torch.bfloat16)
+            outs.append(x)
         return torch.stack(outs)
 
 

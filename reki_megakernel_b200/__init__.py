@@ -7,11 +7,14 @@ CPU fallback.
 from .synthetic import ExpertDims, ExpertWeights, StepInputs, make_inputs, make_model, make_past, make_weights
 
 __all__ = ["ExpertDims", "ExpertWeights", "StepInputs", "make_inputs", "make_model", "make_past", "make_weights",
-           "ExpertMegakernel", "install"]
+           "ExpertMegakernel", "install", "RegisterPrepare", "register_prepare"]
 
 
 def __getattr__(name):
     if name in ("ExpertMegakernel", "install"):
         from . import mk_expert
         return getattr(mk_expert, name)
+    if name in ("RegisterPrepare", "register_prepare"):
+        from . import prepare
+        return getattr(prepare, name)
     raise AttributeError(name)

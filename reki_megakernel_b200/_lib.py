@@ -63,6 +63,7 @@ SIGNATURES = {
     "mkx_clear_error": (C.c_int, [P]),
     "mkx_set_timeout_ns": (C.c_int, [P, C.c_ulonglong]),
     "mkx_set_fault_injection": (C.c_int, [P, C.c_int]),
+    "mkx_set_launch_sequence": (C.c_int, [P, C.c_uint]),
     "mkx_launch_shape": (C.c_int, [P, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
     "mkx_run_static": (C.c_int, [C.POINTER(Dims), C.POINTER(PackedWeights), C.POINTER(StepInputs), P, P]),
     "mkx_last_cuda_error": (C.c_char_p, []),

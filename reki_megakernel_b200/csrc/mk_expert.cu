@@ -1292,6 +1292,53 @@ __device__ __forceinline__ int stage_attention(const Params& p, Cta& c, const bo
   return 0;
 }
 
+// Exchange words this launch will not rewrite, set to tag 0 (never a valid tag: instance + 1 is
+// in 1..4095). A tag repeats after 2^20 launches (the sequence number has 20 bits left above the
+// instance); a word last written that long ago -- a row >= T of a launch with more action rows, an
+// action-state word >= action_dim, a parity that a short launch never uses -- would otherwise pass
+// for fresh in a later launch whose geometry reads it. Each CTA clears only words it alone produces
+// (the same ownership as its epilogues) and that no stage of this launch writes or reads, so the
+// stores race with nothing; they run at the launch's exit (also after a failed wait), and the next
+// launch on the stream sees them. After every launch each word holds 0 or a tag of that launch or
+// of an earlier one that a later launch has not overwritten.
+__device__ void clear_stale_words(const Params& p, const Cta& c) {
+  const bool par1 = p.n_steps * p.L >= 2;  // parity 1 is used by instances 1, 3, ...
+  int xpar = 0;                             // bit mask: parities of the action-state words of steps 0..n-2
+  for (int s = 0; s + 1 < p.n_steps && s < 2; ++s) xpar |= 1 << ((s * p.L + p.L - 1) & 1);
+  auto clear_owned = [&](int b, int w0, int nw, int rw, bool perm) {  // nw <= NT words per row
+    if (c.tid >= nw) return;
+    const int pos = perm ? word_pos(w0 + c.tid) : w0 + c.tid;
+#pragma unroll 1
+    for (int par = 0; par < 2; ++par) {
+      u64* col = p.xb[b] + (size_t)par * TP * rw + pos;
+#pragma unroll 1
+      for (int n = (par == 0 || par1) ? p.T : 0; n < TP; ++n) st_volatile(col + (size_t)n * rw, 0ull);
+    }
+  };
+  clear_owned(B_QKV, c.r0_qkv >> 1, c.R_qkv >> 1, QKVWORDS, true);
+  clear_owned(B_H2, c.c0 >> 1, c.R_h >> 1, HWORDS, true);
+  clear_owned(B_QCA, c.c0 >> 1, c.R_h >> 1, HWORDS, true);
+  clear_owned(B_H3, c.c0 >> 1, c.R_h >> 1, HWORDS, true);
+  clear_owned(B_HOUT, c.c0 >> 1, c.R_h >> 1, HWORDS, true);
+  clear_owned(B_G, c.u0 >> 1, c.R_gu >> 1, p.I >> 1, true);
+  clear_owned(B_DP, c.dgrp * H + c.d0, c.R_dp, DPWORDS, false);
+  // attention outputs: unit u = (head u % NH, row u / NH), produced by CTA u % G
+  for (int u = c.cta; u < NH * TP; u += c.G) {
+    const int n = u / NH, h = u % NH;
+    for (int par = 0; par < 2; ++par) {
+      if (n < p.T && (par == 0 || par1)) continue;
+      if (c.tid < 64)
+        st_volatile(p.xb[c.tid < 32 ? B_Y : B_YCA] + (size_t)par * TP * HWORDS + (size_t)n * HWORDS + h * 32 + (c.tid & 31),
+                    0ull);
+    }
+  }
+  // action state: row n produced by CTA n (words a < action_dim, intermediate steps only)
+  if (c.cta < TP && c.tid < 2 * XWORDS) {
+    const int n = c.cta, par = c.tid / XWORDS, a = c.tid % XWORDS;
+    if (!(((xpar >> par) & 1) && n < p.T && a < p.adim)) st_volatile(p.xb[B_X] + (size_t)par * TP * XWORDS + (size_t)n * XWORDS + a, 0ull);
+  }
+}
+
 // Euler step tail of step s: velocity rows (CTAs n < T), action-state exchange, and every CTA's
 // in-projection of the next step's h0 into X.
 template <typename ModT>
@@ -1405,6 +1452,7 @@ __global__ void __launch_bounds__(NT, 1) expert_kernel(const __grid_constant__ P
   }
 
 drain:
+  clear_stale_words(p, c);
   // Normal exit: nothing is in flight. After a failed wait: drain every issued bulk copy (bounded).
   __syncthreads();
   if (c.tid == 0) {
@@ -1843,6 +1891,14 @@ extern "C" mkx_status mkx_set_fault_injection(mkx_handle* h, int stage) {
   return MKX_OK;
 }
 
+extern "C" mkx_status mkx_set_launch_sequence(mkx_handle* h, unsigned int seq) {
+  if (!h) return MKX_ERR_INVALID_ARG;
+  DeviceScope dev_scope(h->device);
+  MKX_CUDA(dev_scope.err);
+  MKX_CUDA(cudaMemcpy(h->base.status + 1, &seq, sizeof(seq), cudaMemcpyHostToDevice));
+  return MKX_OK;
+}
+
 extern "C" mkx_status mkx_launch_shape(const mkx_handle* h, int* grid, int* smem_bytes) {
   if (!h) return MKX_ERR_INVALID_ARG;
   if (grid) *grid = h->G;
@@ -1907,6 +1963,7 @@ mkx_status static_setup(int dev, StaticDevice** out) {
 extern "C" mkx_status mkx_run_static(const mkx_dims* dims, const mkx_packed_weights* w, const mkx_step_inputs* in,
                                      int* err_out, cudaStream_t stream) {
   if (!dims || !w || !in) return MKX_ERR_INVALID_ARG;
+  if (err_out && (reinterpret_cast<uintptr_t>(err_out) & 3u)) return static_fail("err_out must be 4-byte aligned", MKX_ERR_INVALID_ARG);
   const mkx_dims d = *dims;
   if (d.H != H || d.NH != NH || d.HD != HD || d.L < 1 || d.L > MKX_MAX_LAYERS || d.I < 128 || d.I % 128 != 0 ||
       d.A < AO || d.A > 32)

@@ -341,6 +341,11 @@ class ExpertMegakernel:
     def set_fault_injection(self, stage: int) -> None:
         _lib.check(self._lib.mkx_set_fault_injection(self._h, int(stage)), "mkx_set_fault_injection")
 
+    def set_launch_sequence(self, seq: int) -> None:
+        """Test hook: the handle's launch sequence number (exchange tags are seq * 4096 + instance + 1
+        in 32 bits, so seq and seq + 2**20 give the same tags)."""
+        _lib.check(self._lib.mkx_set_launch_sequence(self._h, int(seq) & 0xFFFFFFFF), "mkx_set_launch_sequence")
+
     def close(self) -> None:
         if getattr(self, "_h", None):
             self._lib.mkx_destroy(self._h)

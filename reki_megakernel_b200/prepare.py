@@ -9,6 +9,7 @@ There is no CPU fallback: the CUDA library must load.
 from __future__ import annotations
 
 import ctypes as C
+from types import SimpleNamespace
 
 import torch
 
@@ -100,3 +101,33 @@ class RegisterPrepare:
             self.close()
         except Exception:
             pass
+
+
+def register_prepare(prepare: RegisterPrepare, ca_src: torch.Tensor, mem_kv, *, T: int, kv_start: int = 0,
+                     SP: int | None = None, out=None):
+    """``register_prepare`` under the reference's name: what the reference megakernel says it reads
+    from Kyutai's step-1 side (``src/mk_expert.py:22-24``: "register_prepare (CA source K/V, cos/sin,
+    cu_seqlens)"), built on the GPU, returned as the ``past`` object ``ExpertMegakernel.run`` takes
+    (``src/mk_expert.py:486-495``).
+
+    ca_src: [S, src_dim] bf16 VLM source rows; mem_kv: per layer (K, V) [PM, NH, HD] bf16 register
+    memory (rows >= kv_start valid, already normed and rotated); T: action rows. Returns
+    ``past.cross_attn_kv`` (per layer K, V [SP, NH, HD], from one tcgen05 launch), and
+    ``past.register_step`` with ``mem_kv``, ``sa_pe`` (RoPE of the action rows at positions
+    PM .. PM + T - 1, after the memory), ``ca_pe`` (positions 0 .. T - 1), ``cu_kv`` = [kv_start, PM]
+    and ``cu_src`` = [0, S] (int32, device). Asynchronous on the current stream; ``out`` = (k, v)
+    reuses K/V buffers (graph capture)."""
+    d, dev = prepare.dims, prepare.device
+    S = ca_src.shape[0]
+    if len(mem_kv) != d.L:
+        raise ValueError(f"mem_kv needs {d.L} (K, V) pairs")
+    PM = mem_kv[0][0].shape[0]
+    if not 0 <= kv_start <= PM:
+        raise ValueError(f"kv_start={kv_start} must be in 0..{PM}")
+    k, v = prepare.run(ca_src, SP=SP, out=out)
+    sa = tuple(t.to(dev) for t in rope_cos_sin(torch.arange(T) + PM, d.HD))
+    ca = tuple(t.to(dev) for t in rope_cos_sin(torch.arange(T), d.HD))
+    step = {"mem_kv": list(mem_kv), "sa_pe": sa, "ca_pe": ca,
+            "cu_kv": torch.tensor([kv_start, PM], dtype=torch.int32, device=dev),
+            "cu_src": torch.tensor([0, S], dtype=torch.int32, device=dev)}
+    return SimpleNamespace(register_step=step, cross_attn_kv=[(k[l], v[l]) for l in range(d.L)])

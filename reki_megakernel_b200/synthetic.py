@@ -117,8 +117,22 @@ def _randn(gen, shape, std, dtype=torch.bfloat16):
     return (torch.randn(shape, generator=gen, dtype=torch.float32) * std).to(dtype)
 
 
-def make_weights(dims: ExpertDims = ExpertDims(), seed: int = 0, std: float = 0.02) -> ExpertWeights:
-    """Random-init expert weights N(0, std) on the CPU, one generator, fixed draw order."""
+OUT_STD = 0.005
+
+
+def make_weights(dims: ExpertDims = ExpertDims(), seed: int = 0, std: float = 0.02,
+                 out_std: float = OUT_STD) -> ExpertWeights:
+    """Random-init expert weights N(0, std) on the CPU, one generator, fixed draw order.
+
+    ``action_out_proj.weight`` is drawn N(0, out_std) from the same stream (default 0.005). A
+    random-init 10-layer expert iterated over 9 Euler steps is far more sensitive to rounding than
+    the trained one: at out_std = 0.02, two correct bf16 implementations (the reference kernel and
+    the bf16 oracle) end 1.05e-2 / 2.9e-3 (max / mean) apart, and the bf16 and fp32 oracles
+    7.8e-3 / 2.4e-3, against 1.56e-3 max for the reference's compiled and eager trained expert
+    (``results/gpus/b200/test_mk.json:8``). The velocity scale set by out_std is what carries that
+    sensitivity into the action chunk; at 0.005 the bf16 and fp32 oracles end 2.2e-3 / 6.4e-4
+    apart, the trained expert's level, so the parity tolerance (max 1e-2, mean 1.5e-3) applies to
+    the chunk as it is. Every other weight is N(0, std)."""
     d = dims
     g = torch.Generator().manual_seed(seed)
     L, H, I, HD, A = d.L, d.H, d.I, d.HD, d.A
@@ -128,7 +142,7 @@ def make_weights(dims: ExpertDims = ExpertDims(), seed: int = 0, std: float = 0.
         wg=_randn(g, (L, I, H), std), wu=_randn(g, (L, I, H), std), wd=_randn(g, (L, H, I), std),
         qn=_randn(g, (L, HD), std), kn=_randn(g, (L, HD), std), qcan=_randn(g, (L, HD), std),
         win=_randn(g, (A, H), std, torch.float32), bin=_randn(g, (H,), std, torch.float32),
-        wout=_randn(g, (A, H), std, torch.float32), bout=_randn(g, (A,), std, torch.float32),
+        wout=_randn(g, (A, H), out_std, torch.float32), bout=_randn(g, (A,), std, torch.float32),
     )
     return ExpertWeights(dims=d, **w)
 

@@ -77,6 +77,7 @@ def test_null_arguments_are_rejected_without_a_device():
     assert lib.mkx_sync_points(None, 9) == -1
     assert lib.mkx_set_timeout_ns(None, 1) == _lib.MKX_ERR_INVALID_ARG
     assert lib.mkx_set_fault_injection(None, 1) == _lib.MKX_ERR_INVALID_ARG
+    assert lib.mkx_set_launch_sequence(None, 1) == _lib.MKX_ERR_INVALID_ARG
     assert lib.mkx_clear_error(None) == _lib.MKX_ERR_INVALID_ARG
     assert lib.mkx_last_error(None, None, None) == _lib.MKX_ERR_INVALID_ARG
     assert lib.mkx_launch_shape(None, None, None) == _lib.MKX_ERR_INVALID_ARG
@@ -84,6 +85,18 @@ def test_null_arguments_are_rejected_without_a_device():
     w = _lib.Weights(*([1] * 14))
     assert lib.mkx_create(C.byref(d), C.byref(w), 0, C.byref(h)) == _lib.MKX_ERR_UNSUPPORTED
     lib.mkx_destroy(None)
+
+
+def test_static_entry_rejects_a_misaligned_error_word_without_a_device():
+    """mkx_run_static copies the launch's 4-byte error word to err_out on the stream; a misaligned
+    err_out would only fail later, asynchronously, so the call rejects it up front."""
+    from reki_megakernel_b200 import _lib
+    lib = _lib.load()
+    d = _lib.Dims(L=10, H=768, NH=12, HD=64, I=3072, A=32, eps=1e-6, qk_eps=1e-6, max_rows=16, grid=0)
+    pw, si = _lib.PackedWeights(), _lib.StepInputs()
+    si.T = 10
+    assert lib.mkx_run_static(C.byref(d), C.byref(pw), C.byref(si), C.c_void_p(0x1002), None) == _lib.MKX_ERR_INVALID_ARG
+    assert b"aligned" in lib.mkx_last_cuda_error()
 
 
 def test_prepare_arguments_are_rejected_without_a_device():

@@ -21,8 +21,15 @@ def test_algorithmic_bytes_per_euler_step():
     assert 9 * per_step == 1_914_105_600        # one launch = Euler steps 2..10
 
 
-def test_traffic_figure_is_read_from_the_profile_summary():
-    t = bench.traffic_from_profile()
-    assert t is not None
-    # ncu's DRAM bytes of one launch: within 1 % of the algorithmic bytes (no re-reads)
-    assert abs(t / 1_914_105_600 - 1.0) < 0.01
+def test_traffic_figure_is_tied_to_the_kernel_sources_it_was_captured_from():
+    """The ncu summary records the sha of the kernel sources it profiled; bench.py reports its
+    traffic figure only while the sources are the same, and says why when they are not."""
+    t, src = bench.traffic_from_profile()
+    text = (ROOT / "profiles" / "expert_kernel_full.md").read_text()
+    recorded = [ln.split(":", 1)[1].split()[0] for ln in text.splitlines() if ln.startswith("kernel_source_sha16:")]
+    if recorded and recorded[0] == bench.kernel_source_sha():
+        assert t is not None and "ncu capture" in src
+        # ncu's DRAM bytes of one launch: within 1 % of the algorithmic bytes (no re-reads)
+        assert abs(t / 1_914_105_600 - 1.0) < 0.01
+    else:
+        assert t is None and "other kernel sources" in src

@@ -3,12 +3,9 @@ with the reference kernel's golden outputs, plus the launch invariants the refer
 (``src/test_mk.py:41-51``: max |d| against the other implementations, barrier-count invariant).
 
 Tolerance: max |d| <= 1e-2 and mean |d| <= 1.5e-3 on the real action dims of
-the normalized chunk. Short loops (2 layers, <= 2 Euler steps) use it as is; the full 90-layer loop
-uses it on the chunk scaled to the normalized range (``_cases.scaled_parity``): over 90 bf16 layers
-with random-init weights any two correct implementations drift apart by ~1e-2 (the reference
-kernel itself is 1.05e-2 / 2.9e-3 away from the bf16 oracle on ``ref_full``). The chaos-free check
-is per layer: every traced layer output is compared with the oracle's layer applied to the
-kernel's own traced input (teacher forcing).
+the chunk, as is, for every loop length (the synthetic action_out_proj is drawn at std 0.005, see
+``synthetic.make_weights``). The rounding-level check is per layer: every traced layer output is
+compared with the oracle's layer applied to the kernel's own traced input (teacher forcing).
 """
 import pytest
 import torch
@@ -16,7 +13,7 @@ import torch
 from oracle.expert_oracle import OracleExpert
 from reki_megakernel_b200.synthetic import ExpertDims, make_inputs, make_past, make_weights
 
-from _cases import GOLDEN_FILES, TOL_MAX, TOL_MEAN, chunk_err, golden_case, scaled_parity
+from _cases import GOLDEN_FILES, TOL_MAX, TOL_MEAN, chunk_err, golden_case
 
 pytestmark = pytest.mark.gpu
 
@@ -55,8 +52,9 @@ def test_full_config_vs_oracle(full):
     inp = make_inputs(dims, poison=True)   # T=10, 9 steps, S=160, 2 of 3 frames
     out = run_mk(mk, inp)
     ref = orc.run(inp)[0]
-    ok, mx, mean, sc = scaled_parity(out, ref, inp.action_dim)
-    assert ok, (mx, mean, sc)
+    mx, mean = chunk_err(out, ref, inp.action_dim)
+    print(f"kernel vs bf16 oracle, BASELINE configs[1]: max {mx:.3e}, mean {mean:.3e}")
+    assert mx <= TOL_MAX and mean <= TOL_MEAN, (mx, mean)
     assert torch.isfinite(out).all()
 
 
@@ -75,12 +73,9 @@ def test_vs_reference_golden(name, full, small):
         mk = ExpertMegakernel(weights=w.to(DEV))
     out = run_mk(mk, inp)
     ref = torch.from_numpy(z["x_out"])
-    if name == "full":
-        ok, mx, mean, sc = scaled_parity(out, ref, inp.action_dim)
-        assert ok, (mx, mean, sc)
-    else:
-        mx, mean = chunk_err(out, ref, inp.action_dim)
-        assert mx <= TOL_MAX and mean <= TOL_MEAN, (mx, mean)
+    mx, mean = chunk_err(out, ref, inp.action_dim)
+    print(f"kernel vs reference kernel ({name}): max {mx:.3e}, mean {mean:.3e}")
+    assert mx <= TOL_MAX and mean <= TOL_MEAN, (mx, mean)
     if name == "layer":  # one layer, one step: every stage's rounding points line up
         assert mx <= 1e-3, mx
 
@@ -224,6 +219,26 @@ def test_cuda_graph_capture(small):
         torch.cuda.synchronize()
         assert torch.equal(out, eager)
     mk.check_device_error()
+
+
+def test_exchange_tags_after_the_sequence_wraps(small):
+    """Exchange tags repeat every 2^20 launches. A launch with 16 action rows, then one with 10 (it
+    clears rows 10-15 of every exchange buffer, which it does not use), then, 2^20 sequence numbers
+    after the first (set through the test hook instead of a million launches), one with 16 rows
+    again: its tags equal the first launch's, and its output must still equal a fresh handle's,
+    bit for bit -- no word of the first launch is taken for one of the third's."""
+    from reki_megakernel_b200.mk_expert import ExpertMegakernel
+    dims, w, mk, _ = small
+    third = make_inputs(dims, T=16, n_steps=1, poison=True, seed=53)
+    fresh = ExpertMegakernel(weights=w.to(DEV))
+    want = run_mk(fresh, third)
+    fresh.close()
+    seq = 5000
+    mk.set_launch_sequence(seq)
+    run_mk(mk, make_inputs(dims, T=16, n_steps=1, poison=True, seed=51))
+    run_mk(mk, make_inputs(dims, T=10, n_steps=1, poison=True, seed=52))
+    mk.set_launch_sequence(seq + (1 << 20))
+    assert torch.equal(run_mk(mk, third), want)
 
 
 def test_timeout_reports_error_and_recovers(small):

@@ -1,8 +1,8 @@
 """The GPU half of a predict after Euler step 1 as one CUDA graph (modulation rows, cross-attention
 K/V, Euler steps 2..N): every replay equals the same three calls made eagerly, bit for bit (all
 three kernels are deterministic), for successive inputs; and the graph's action chunk matches the
-CPU expert oracle fed with the same modulation rows and K/V, under the north-star tolerance scaled
-to the synthetic chunk's range as in the other full-size parity tests (``_cases.scaled_parity``)."""
+CPU expert oracle fed with the same modulation rows and K/V, under the north-star tolerance (max
+1e-2, mean 1.5e-3 on the real action dims)."""
 import pytest
 import torch
 
@@ -59,7 +59,7 @@ def test_graph_replays_equal_eager_calls(parts):
 
 
 def test_graph_matches_the_expert_oracle(parts):
-    from _cases import scaled_parity
+    from _cases import TOL_MAX, TOL_MEAN, chunk_err
     from oracle.expert_oracle import OracleExpert
     from reki_megakernel_b200.predict import PredictGraph
     d, mk, rp, sm = parts
@@ -79,6 +79,6 @@ def test_graph_matches_the_expert_oracle(parts):
     ref_in.vca = pg.v.cpu()[None]
     ref_in.dt = pg.dt.cpu().reshape(1)
     ref = OracleExpert(make_weights(d, seed=0), "bf16").run(ref_in)[0]
-    ok, mx, mean, sc = scaled_parity(got[0].cpu(), ref, inp.action_dim)
-    assert ok, (mx, mean, sc)
+    mx, mean = chunk_err(got[0].cpu(), ref, inp.action_dim)
+    assert mx <= TOL_MAX and mean <= TOL_MEAN, (mx, mean)
     assert torch.isfinite(got).all()

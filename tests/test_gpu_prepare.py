@@ -88,3 +88,37 @@ def test_prepare_graph_capture_and_feeds_the_expert():
     assert torch.equal(k, eager[0]) and torch.equal(v, eager[1])
     assert k.shape == (d.L, 160, d.NH, d.HD) and k.stride(1) == d.NH * d.HD   # one K row per source row
     rp.close()
+
+
+def test_register_prepare_callable_builds_the_expert_past():
+    """``register_prepare(prepare, src, mem_kv, T=..., kv_start=...)`` returns the ``past`` the expert
+    reads: its K/V equal ``RegisterPrepare.run``'s, its tables and cu_seqlens are the ones the
+    synthetic inputs use, and the expert run on it equals the run on an equivalent hand-built past."""
+    from reki_megakernel_b200.mk_expert import ExpertMegakernel
+    from reki_megakernel_b200.prepare import RegisterPrepare, register_prepare
+    from reki_megakernel_b200.synthetic import make_inputs, make_past, make_weights
+    d = ExpertDims(L=2, I=1024)
+    S = 96
+    rp = RegisterPrepare(make_prepare_weights(d, seed=0).to(DEV))
+    src = make_source(S, d.src_dim, seed=4).to(DEV)
+    inp = make_inputs(d, T=10, n_steps=2, S=S, SP=S, seed=4).to(DEV)
+    mem = [(inp.memk[0, l], inp.memv[0, l]) for l in range(d.L)]
+    past = register_prepare(rp, src, mem, T=10, kv_start=int(inp.kv_start[0]))
+    k, v = rp.run(src)
+    for l in range(d.L):
+        assert torch.equal(past.cross_attn_kv[l][0], k[l]) and torch.equal(past.cross_attn_kv[l][1], v[l])
+    inp.kca, inp.vca = k[None], v[None]
+    ref_past = make_past(inp)
+    for key in ("sa_pe", "ca_pe"):
+        for a, b in zip(past.register_step[key], ref_past.register_step[key]):
+            assert torch.equal(a, b)
+    for key in ("cu_kv", "cu_src"):
+        assert torch.equal(past.register_step[key], ref_past.register_step[key])
+    mk = ExpertMegakernel(weights=make_weights(d, seed=0).to(DEV))
+    a = mk.run(inp.x[:1], inp.mods[0], inp.dt[:1], past, inp.action_dim)
+    b = mk.run(inp.x[:1], inp.mods[0], inp.dt[:1], ref_past, inp.action_dim)
+    torch.cuda.synchronize()
+    mk.check_device_error()
+    assert torch.equal(a, b)
+    mk.close()
+    rp.close()

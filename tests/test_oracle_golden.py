@@ -10,13 +10,13 @@ oracle (``oracle/expert_oracle.py``, mode "bf16") runs on the CPU.
   rounding (<= 1e-6) and >= 99.9 % of every scratch buffer is bit-identical (the rest one-ulp flips
   from a different fp32 summation order: within 2^-8 of the buffer's largest magnitude);
 * 2 layers x 3 steps and the full configuration (10 layers x 9 steps): the one-ulp flips compound
-  through the Euler loop, so the chunk is checked with the north-star tolerance (the full one scaled
-  to the normalized-action range, ``_cases.scaled_parity``).
+  through the Euler loop, so the chunk is checked with the north-star tolerance (max 1e-2, mean
+  1.5e-3 on the real action dims, as is).
 """
 import pytest
 import torch
 
-from _cases import GOLDEN_FILES, TOL_MAX, TOL_MEAN, bf16_from_u16, chunk_err, golden_case, scaled_parity
+from _cases import GOLDEN_FILES, TOL_MAX, TOL_MEAN, bf16_from_u16, chunk_err, golden_case
 from oracle.expert_oracle import OracleExpert
 
 BUFFERS = (("h", "h_last"), ("h2", "h2_last"), ("h3", "h3_last"), ("qkv", "qkv_last"), ("qca", "qca_last"),
@@ -53,6 +53,6 @@ def test_two_layers_three_steps_within_tolerance():
 
 def test_full_configuration_within_tolerance():
     inp, z, x, _ = _run("full")
-    ok, mx, mean, sc = scaled_parity(x, torch.from_numpy(z["x_out"]), inp.action_dim)
-    assert ok, (mx, mean, sc)
+    mx, mean = chunk_err(x, torch.from_numpy(z["x_out"]), inp.action_dim)
+    assert mx <= TOL_MAX and mean <= TOL_MEAN, (mx, mean)
     assert int(z["barriers"]) == int(z["expected_barriers"])  # the reference run walked every barrier
