@@ -547,6 +547,145 @@ def job_episodes_per_s(world: int, batch: int, ms_per_step: float) -> float:
     return world * batch * 1000.0 / ms_per_step
 
 
+def batch_algorithmic(dims, B: int, T: int, S: int, PM: int, SP: int, n_steps: int = 9):
+    """(HBM bytes, FLOPs) one batched predict must move / compute: the weights and fp32 projections once
+    per Euler step for all B episodes, and per episode and step its modulation row, register memory
+    K/V (PM rows) and cross-attention K/V (S rows) of every layer; FLOPs of the dense stages
+    (2 x rows x weights) and of the attention (scores and P V)."""
+    L, H, I, A, HD = dims.L, dims.H, dims.I, dims.A, dims.HD
+    wbytes = 2 * L * (3 * H * H + 3 * H * I + 3 * H * H) + 4 * 2 * A * H + 2 * 3 * L * HD
+    per_ep = dims.MODW * 2 + L * (PM + S) * H * 2 * 2
+    hbm = n_steps * (wbytes + B * per_ep)
+    params = L * (3 * H * H + 3 * H * H + 3 * H * I)
+    flops = n_steps * (2.0 * B * T * params + B * L * 4.0 * T * (PM + T + S) * H)
+    return hbm, flops
+
+
+def run_batch(args, rank: int, world: int):
+    """B episodes per GPU through the batch path (BatchedExpert: one weight stream
+    per Euler step for all of them, tcgen05 GEMMs over the stacked action rows). One step = one
+    predict of all B episodes, replayed as a CUDA graph; value = episodes/s over the job."""
+    from reki_megakernel_b200.batch import BatchedExpert
+    from reki_megakernel_b200.synthetic import ExpertDims, make_inputs, make_weights
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dims = ExpertDims()
+    B = args.batch
+    bx = BatchedExpert(make_weights(dims, seed=0).to(dev), max_episodes=B)
+    # this rank's episodes rank * B .. rank * B + B - 1, each seeded by its global index
+    host = make_inputs(dims, B=B, S=args.S, seed=1000 * rank * B, noise_seed=1234 + rank * B)
+    inp = host.to(dev)
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        for _ in range(2):
+            bx.run(inp)
+    torch.cuda.current_stream(dev).wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = bx.run(inp)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    for _ in range(args.warmup):
+        g.replay()
+    torch.cuda.synchronize(dev)
+    bx.check_device_error()
+    clocks = Clocks(local)
+    clocks.start()
+    time.sleep(0.3)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize(dev)
+    t_wall = time.perf_counter()
+    for a, b in evs:
+        flush.fill_(1)
+        a.record(stream)
+        g.replay()
+        b.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    wall = time.perf_counter() - t_wall
+    clk = clocks.stop()
+    bx.check_device_error()
+    per = [a.elapsed_time(b) for a, b in evs]
+    ms = statistics.mean(per)
+    # end to end: every step copies all B episodes' inputs from pinned host memory, runs, reads back
+    pinned = {k: (v.contiguous().pin_memory() if isinstance(v, torch.Tensor) else v) for k, v in host.__dict__.items()}
+    h2d = sum(v.numel() * v.element_size() for v in pinned.values() if isinstance(v, torch.Tensor))
+    out_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    d2h = out_h.numel() * out_h.element_size()
+    dev_t = {k: v for k, v in inp.__dict__.items() if isinstance(v, torch.Tensor)}
+
+    def e2e_call():
+        for k, v in dev_t.items():
+            v.copy_(pinned[k], non_blocking=True)
+        o = bx.run(inp)
+        out_h.copy_(o, non_blocking=True)
+
+    for _ in range(3):
+        e2e_call()
+    torch.cuda.synchronize(dev)
+    e2e_ms = []
+    for _ in range(max(5, args.steps // 4)):
+        flush.fill_(1)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        e2e_call()
+        b.record(stream)
+        b.synchronize()
+        e2e_ms.append(a.elapsed_time(b))
+    bx.check_device_error()
+    ms_max, e2e_max = max_over_ranks([ms, statistics.mean(e2e_ms)], world, dev)
+    if rank != 0:
+        return
+    PM, SP = host.memk.shape[2], host.kca.shape[2]
+    hbm_bytes, flops = batch_algorithmic(dims, B, host.x.shape[1], args.S, PM - int(host.kv_start[0]), SP)
+    hbm, peak_kind = peaks()
+    tflops_peak = bf16_peak()
+    achieved_gbs = hbm_bytes / (ms * 1e-3) / 1e9
+    achieved_tf = flops / (ms * 1e-3) / 1e12
+    tensor_bound = achieved_tf / tflops_peak[0] > achieved_gbs / hbm
+    roof = ({"bound": "tensor", "achieved": achieved_tf, "peak": tflops_peak[0], "unit": "TFLOP/s",
+             "frac": achieved_tf / tflops_peak[0], "peak_kind": tflops_peak[1]} if tensor_bound else
+            {"bound": "hbm", "achieved": achieved_gbs, "peak": hbm, "unit": "GB/s", "frac": achieved_gbs / hbm,
+             "peak_kind": f"{peak_kind} (hbm copy, burst)"})
+    roof.update({"traffic": None, "traffic_source": "not captured for the batch path",
+                 "algorithmic_bytes_per_step": hbm_bytes, "flops_per_step": flops,
+                 "hbm_gbs": achieved_gbs, "tflops": achieved_tf})
+    line = {
+        "metric": METRIC, "value": job_episodes_per_s(world, B, ms_max), "unit": "episodes/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
+        "ms_per_predict": ms_max, "ms_per_step_p50": statistics.median(per),
+        "ms_per_step_p99": sorted(per)[min(len(per) - 1, int(0.99 * len(per)))],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded weights, BASELINE configs[4] shapes, episodes seeded by index)",
+        "config": dict(bench_config(args, world),
+                       workload=f"REKI expert Euler steps 2-10 (BASELINE configs[4]): {B} episodes per GPU in one "
+                                "batched predict (one weight stream, tcgen05 GEMMs over the stacked action rows)"),
+        "roofline": roof,
+        "e2e": {"value": job_episodes_per_s(world, B, e2e_max), "unit": "episodes/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_max},
+        "gpu_launches": args.steps * bx.launches(B, host.x.shape[1], 9),
+        "clocks": clk,
+        "wall_s_timed_region": wall,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def bf16_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["bf16_tflops"]), "measured (cuBLAS bf16, burst)"
+    return 1590.0, "fallback"
+
+
 def run_mk(args, rank: int, world: int):
     from types import SimpleNamespace
     from reki_megakernel_b200.mk_expert import ExpertMegakernel
@@ -692,7 +831,8 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="mk", choices=["mk", "reference"])
-    ap.add_argument("--batch", type=int, default=1, help="episodes per GPU (one batch-1 launch each per step)")
+    ap.add_argument("--batch", type=int, default=1,
+                    help="episodes per GPU; > 1 runs the batch path (one weight stream for all of them)")
     ap.add_argument("--S", type=int, default=160, help="cross-attention source rows (BASELINE configs[3]: 128-1024)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -726,6 +866,8 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, rank, world)
+        elif args.batch > 1:
+            run_batch(args, rank, world)
         else:
             run_mk(args, rank, world)
     finally:

@@ -1,5 +1,5 @@
-"""ctypes binding of ``libmkx.so`` (declarations in ``include/mkx.h``, ``include/mkx_prepare.h`` and
-``include/mkx_mods.h``).
+"""ctypes binding of ``libmkx.so`` (declarations in ``include/mkx.h``, ``include/mkx_prepare.h``,
+``include/mkx_mods.h`` and ``include/mkx_batch.h``).
 
 The library is built in-tree by ``reki_megakernel_b200.build``. There is no fallback: if the
 library is missing or does not load, importing this module raises.
@@ -46,6 +46,13 @@ class PackedWeights(C.Structure):
     _fields_ = [("w", P * 6), ("nrm", P), ("tailw", P), ("wout", P)]
 
 
+class BatchInputs(C.Structure):
+    _fields_ = [("x_in", P), ("x_out", P), ("mods", P), ("dt", P), ("memk", P), ("memv", P), ("kv_start", P),
+                ("mem_rows", C.c_int), ("kca", P), ("vca", P), ("src_rows", P), ("ca_rows", C.c_int),
+                ("sa_cos", P), ("sa_sin", P), ("ca_cos", P), ("ca_sin", P), ("B", C.c_int), ("T", C.c_int),
+                ("n_steps", C.c_int), ("action_dim", C.c_int)]
+
+
 class PrepDims(C.Structure):
     _fields_ = [("L", C.c_int), ("H", C.c_int), ("NH", C.c_int), ("HD", C.c_int), ("src_dim", C.c_int),
                 ("eps", C.c_float)]
@@ -69,6 +76,13 @@ SIGNATURES = {
     "mkx_last_cuda_error": (C.c_char_p, []),
     "mkx_h2d_copies": (C.c_int, [C.c_int, P, P, P, P]),
     "mkx_destroy": (None, [P]),
+    "mkx_batch_create": (C.c_int, [C.POINTER(Dims), C.POINTER(Weights), C.c_int, C.c_int, C.POINTER(P)]),
+    "mkx_batch_run": (C.c_int, [P, C.POINTER(BatchInputs), P]),
+    "mkx_batch_last_error": (C.c_int, [P, C.POINTER(C.c_int)]),
+    "mkx_batch_launches": (C.c_int, [P, C.c_int, C.c_int, C.c_int]),
+    "mkx_batch_last_cuda_error": (C.c_char_p, []),
+    "mkx_batch_copy_state": (C.c_int, [P, C.c_int, P, C.c_size_t]),
+    "mkx_batch_destroy": (None, [P]),
     "mkx_prep_create": (C.c_int, [C.POINTER(PrepDims), P, P, C.c_int, C.POINTER(P)]),
     "mkx_prep_run": (C.c_int, [P, P, C.c_int, P, P, P, P, C.c_int, P]),
     "mkx_prep_last_error": (C.c_int, [P, C.POINTER(C.c_int)]),
@@ -134,5 +148,6 @@ def check(status: int, where: str) -> None:
     if status != MKX_OK:
         detail = ""
         if status == MKX_ERR_CUDA:
-            detail = (load().mkx_last_cuda_error() or b"").decode(errors="replace")
+            fn = load().mkx_batch_last_cuda_error if where.startswith("mkx_batch") else load().mkx_last_cuda_error
+            detail = (fn() or b"").decode(errors="replace")
         raise MkxError(where, status, detail)

@@ -21,6 +21,7 @@
 
 #include "mkx_prepare.h"
 #include "mkx_device.cuh"
+#include "mkx_tma.cuh"
 
 namespace mkxp {
 using namespace mkx;
@@ -56,14 +57,6 @@ __device__ __forceinline__ bool wait_bounded(uint64_t* bar, uint32_t parity, uns
   while (!mbar_try_wait(bar, parity))
     if (globaltimer() - t0 > limit) return false;
   return true;
-}
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          smem_u32(dst)),
-      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
 }
 
 __device__ __forceinline__ void record(const PrepParams& p, int code) { atomicCAS(p.status, 0, code); }
@@ -250,36 +243,6 @@ __global__ void prep_pack_kernel(const uint16_t* __restrict__ w, uint16_t* __res
 }
 
 // ---------------------------------------------------------------------------------------------
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encoder() {
-  static EncodeTiledFn fn = nullptr;
-  if (!fn) {
-    void* f = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(f);
-  }
-  return fn;
-}
-
-// bf16 matrix [rows][cols] (row-major), box of 64 columns x box_rows rows, 128-byte swizzle,
-// out-of-range rows read as zero.
-static bool encode_bf16(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
-  EncodeTiledFn fn = encoder();
-  if (!fn) return false;
-  const cuuint64_t dims[2] = {cols, rows};
-  const cuuint64_t strides[1] = {cols * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)BK, box_rows};
-  const cuuint32_t estr[2] = {1, 1};
-  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 }  // namespace mkxp
 
 struct mkx_prep_handle {
@@ -342,7 +305,7 @@ extern "C" mkx_status mkx_prep_run(mkx_prep_handle* h, const uint16_t* src, int 
   if (dev_scope.err != cudaSuccess) return MKX_ERR_CUDA;
   const int ntok = S >= MAXN ? MAXN : ((S + 15) / 16) * 16;
   CUtensorMap ts;
-  if (!encode_bf16(&ts, src, (uint64_t)S, (uint64_t)h->d.src_dim, (uint32_t)ntok)) return MKX_ERR_CUDA;
+  if (!encode_bf16_sw128(&ts, src, (uint64_t)S, (uint64_t)h->d.src_dim, (uint32_t)ntok)) return MKX_ERR_CUDA;
   // as many ring stages as fit next to the alignment slack and the barriers (the transposed
   // accumulator tile reuses the ring; it always fits in 2 stages), at least 80 KB in total: at most
   // 2 CTAs per SM, so their 2 x 256 TMEM columns always fit the SM's 512 and no allocation waits

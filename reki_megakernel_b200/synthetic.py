@@ -20,6 +20,7 @@ published shapes (MODW = 3L*3H + 2H; 31 M cross-attention projection weights) an
 """
 from __future__ import annotations
 
+import functools
 import math
 from dataclasses import dataclass, field
 from types import SimpleNamespace
@@ -168,17 +169,39 @@ def step_modulations(dims: ExpertDims, num_steps: int, state: torch.Tensor, seed
     linear embedding of the proprio state, SiLU, then one Linear to MODW = 3L*3H + 2H values per step
     ([scale, shift, gate] for SA, CA and MLP of each layer, then [scale, shift] of the final norm).
     Returns (mods [N, MODW] bf16, dt scalar fp32 = 1/N)."""
-    g = torch.Generator().manual_seed(seed + 7)
-    H = dims.H
-    w_t = torch.randn((H, 256), generator=g) * 0.02
-    w_s = torch.randn((H, state.numel()), generator=g) * 0.02
-    w_m = torch.randn((dims.MODW, H), generator=g) * 0.02
-    b_m = torch.randn((dims.MODW,), generator=g) * 0.02
+    w_t, w_s, w_m, b_m = _modulation_net(dims, state.numel(), seed)
     t = 1.0 - torch.arange(num_steps, dtype=torch.float32) / num_steps
     e = _timestep_embedding(t) @ w_t.T + (state.float().reshape(1, -1) @ w_s.T)
     e = e * 8.0  # unit-scale conditioning
     mods = torch.nn.functional.silu(e) @ w_m.T + b_m
     return mods.to(torch.bfloat16), torch.tensor(1.0 / num_steps, dtype=torch.float32)
+
+
+@functools.lru_cache(maxsize=2)
+def _modulation_net(dims: ExpertDims, sdim: int, seed: int):
+    """Weights of the restated modulation network (one generator, fixed draw order), drawn once per
+    (dims, state width, seed) and shared by every episode."""
+    g = torch.Generator().manual_seed(seed + 7)
+    H = dims.H
+    w_t = torch.randn((H, 256), generator=g) * 0.02
+    w_s = torch.randn((H, sdim), generator=g) * 0.02
+    w_m = torch.randn((dims.MODW, H), generator=g) * 0.02
+    b_m = torch.randn((dims.MODW,), generator=g) * 0.02
+    return w_t, w_s, w_m, b_m
+
+
+@functools.lru_cache(maxsize=2)
+def _prepare_net(dims: ExpertDims, src_dim: int, seed: int):
+    """Per-layer (Wk, Wv, kn) of the restated K/V preparation, drawn once per (dims, source width,
+    seed) in the order register_prepare_cpu has always drawn them."""
+    g = torch.Generator().manual_seed(seed + 11)
+    out = []
+    for _ in range(dims.L):
+        wk = torch.randn((dims.H, src_dim), generator=g) * 0.02
+        wv = torch.randn((dims.H, src_dim), generator=g) * 0.02
+        kn = torch.randn((dims.HD,), generator=g) * 0.02
+        out.append((wk, wv, kn))
+    return out
 
 
 def _rms(x, eps):
@@ -193,14 +216,12 @@ def register_prepare_cpu(dims: ExpertDims, src: torch.Tensor, seed: int = 0, SP:
     L, H, NH, HD = dims.L, dims.H, dims.NH, dims.HD
     S = src.shape[0]
     SP = SP or S
-    g = torch.Generator().manual_seed(seed + 11)
     k_out = torch.zeros(L, SP, NH, HD, dtype=torch.bfloat16)
     v_out = torch.zeros(L, SP, NH, HD, dtype=torch.bfloat16)
     cos, sin = rope_cos_sin(torch.arange(S), HD)
+    net = _prepare_net(dims, src.shape[1], seed)
     for l in range(L):
-        wk = torch.randn((H, src.shape[1]), generator=g) * 0.02
-        wv = torch.randn((H, src.shape[1]), generator=g) * 0.02
-        kn = torch.randn((HD,), generator=g) * 0.02
+        wk, wv, kn = net[l]
         k = (src.float() @ wk.T).reshape(S, NH, HD)
         v = (src.float() @ wv.T).reshape(S, NH, HD)
         k = _rms(k, eps) * (1.0 + kn)
