@@ -410,6 +410,7 @@ struct AttnParams {
   const float* wq;       // [HD] 1 + q norm weight (SA q / CA q)
   const float* wk;       // [HD] 1 + k norm weight (SA own keys)
   int T;
+  int kcap;              // SA: key rows of the shared K / V tiles (PM + T rounded up to 64)
   float qk_eps, scale;
 };
 
@@ -424,7 +425,7 @@ __global__ void __launch_bounds__(32 * ATT_WARPS) bt_attention(const __grid_cons
   const int e = blockIdx.x / NH, h = blockIdx.x % NH;
   uint16_t* Qs = reinterpret_cast<uint16_t*>(asmem);             // [16][KS]
   uint16_t* Ks = Qs + 16 * KS;                                    // SA: [SA_MAXK][KS]; CA: [2][64][KS]
-  uint16_t* Vs = Ks + (SA ? SA_MAXK : 2 * CA_BLK) * KS;
+  uint16_t* Vs = Ks + (SA ? p.kcap : 2 * CA_BLK) * KS;
   const uint16_t* kb = p.kb + (size_t)e * p.kv_ep + h * HD;
   const uint16_t* vb = p.vb + (size_t)e * p.kv_ep + h * HD;
   const uint32_t zero = 0u;
@@ -773,9 +774,10 @@ struct mkx_batch_handle {
   size_t ws_floats;
   int* status;
   unsigned long long timeout_ns;
-  // tensor maps of the B operands, per token tile size (0: none yet)
-  int map_ntok;
-  CUtensorMap map_a, map_y, map_g;
+  // tensor maps of the GEMM B operands (AdaRMS rows, attention output, gate/up product) per token
+  // tile size ntok = 16 (k + 1), encoded on first use
+  bool map_ok[3][MAXN / 16];
+  CUtensorMap maps[3][MAXN / 16];
 };
 
 static mkx_status batch_fail(cudaError_t e, const char* what) {
@@ -872,13 +874,6 @@ extern "C" mkx_status mkx_batch_create(const mkx_dims* dims, const mkx_weights* 
 }
 
 namespace {
-// Token tile: as many equal tiles of <= 256 rows (a multiple of 16) as M needs.
-int token_tile(int M) {
-  const int nt = (M + MAXN - 1) / MAXN;
-  const int per = (M + nt - 1) / nt;
-  return ((per + 15) / 16) * 16;
-}
-
 // Launch with the programmatic-dependent attribute (the kernel waits for its predecessor itself).
 template <typename... KArgs, typename... Args>
 cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
@@ -895,6 +890,35 @@ cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, 
   return cudaLaunchKernelEx(&cfg, k, args...);
 }
 
+// Token tile of a GEMM with `ntiles` feature tiles: about one CTA per SM (each token tile re-reads the
+// weight tile from L2, not HBM), a multiple of 16 rows, at most 256.
+int gemm_token_tile(int M, int ntiles, int sms) {
+  int tt = (sms + ntiles - 1) / ntiles;
+  if (tt < 1) tt = 1;
+  int per = (M + tt - 1) / tt;
+  if (per > MAXN) per = MAXN;
+  per = ((per + 15) / 16) * 16;
+  const int nt = (M + per - 1) / per;  // balance the tiles
+  return (((M + nt - 1) / nt) + 15) / 16 * 16;
+}
+
+struct GemmLaunch {
+  int stages, smem;
+};
+// Ring stages for a token tile: as many as fit next to the barriers (and, gated epilogues, the
+// residual tile); the transposed accumulator tile reuses the ring. >= 80 KB: at most 2 CTAs
+// (2 x 256 TMEM columns) per SM, so no TMEM allocation waits. false if the accumulator tile does not fit.
+bool gemm_launch_shape(int ntok, bool residual, GemmLaunch* out) {
+  const int stage_bytes = A_BYTES + ntok * BK * 2, slack = 1024 + 256, extra = residual ? ntok * BM * 2 : 0;
+  int st = (SMEM_BUDGET - slack - extra) / stage_bytes;
+  if (st > MAX_STAGES) st = MAX_STAGES;
+  if (st < 2 || ((ntok + 31) / 32) * 32 * TS * 4 > st * stage_bytes) return false;
+  out->stages = st;
+  out->smem = st * stage_bytes + slack + extra;
+  if (out->smem < 80 * 1024) out->smem = 80 * 1024;
+  return true;
+}
+
 // K splits of the down projection: enough CTAs to cover the SMs, >= 4 k tiles (256 K) each.
 int down_splits(const GemmShape& s, int ttiles, int sms) {
   const int ctas = s.ntiles * ttiles;
@@ -907,10 +931,25 @@ int down_splits(const GemmShape& s, int ttiles, int sms) {
 
 extern "C" int mkx_batch_launches(const mkx_batch_handle* h, int B, int T, int n_steps) {
   if (!h || B < 1 || B > h->max_ep || T < 1 || T > TPMAX || n_steps < 1) return -1;
-  const int M = B * T, ntok = token_tile(M), ttiles = (M + ntok - 1) / ntok;
+  const int M = B * T, ntok = gemm_token_tile(M, H / BM, h->sms), ttiles = (M + ntok - 1) / ntok;
   const int reduce = down_splits(gemm_shape(G_D, h->d.I), ttiles, h->sms) > 1 ? 1 : 0;
   return 1 + n_steps * ((11 + reduce) * h->d.L + 1);
 }
+
+namespace {
+// The tensor map of B-operand buffer `buf` (0 AdaRMS rows, 1 attention output, 2 gate/up product) for a
+// token tile of ntok rows (box 64 columns x ntok rows, 128-byte swizzle); nullptr if encoding fails.
+const CUtensorMap* token_map(mkx_batch_handle* h, int buf, int ntok) {
+  const int k = ntok / 16 - 1;
+  if (!h->map_ok[buf][k]) {
+    void* base = buf == 0 ? (void*)h->a : (buf == 1 ? (void*)h->y : (void*)h->g);
+    const uint64_t cols = buf == 2 ? (uint64_t)h->d.I : (uint64_t)H;
+    if (!encode_bf16_sw128(&h->maps[buf][k], base, (uint64_t)h->Mp_max, cols, (uint32_t)ntok)) return nullptr;
+    h->map_ok[buf][k] = true;
+  }
+  return &h->maps[buf][k];
+}
+}  // namespace
 
 extern "C" mkx_status mkx_batch_run(mkx_batch_handle* h, const mkx_batch_inputs* in, cudaStream_t stream) {
   if (!h || !in) return MKX_ERR_INVALID_ARG;
@@ -933,40 +972,25 @@ extern "C" mkx_status mkx_batch_run(mkx_batch_handle* h, const mkx_batch_inputs*
   if (dev_scope.err != cudaSuccess) return batch_fail(dev_scope.err, "cudaSetDevice");
   const int L = d.L, I = d.I, A = d.A, T = in->T, B = in->B;
   const int M = B * T, Mp = ((M + 15) / 16) * 16;
-  const int ntok = token_tile(M), ttiles = (M + ntok - 1) / ntok;
-  if (h->map_ntok != ntok) {
-    if (!encode_bf16_sw128(&h->map_a, h->a, (uint64_t)h->Mp_max, H, ntok) ||
-        !encode_bf16_sw128(&h->map_y, h->y, (uint64_t)h->Mp_max, H, ntok) ||
-        !encode_bf16_sw128(&h->map_g, h->g, (uint64_t)h->Mp_max, (uint64_t)I, ntok)) {
-      snprintf(g_batch_err, sizeof(g_batch_err), "cuTensorMapEncodeTiled failed");
-      return MKX_ERR_CUDA;
-    }
-    h->map_ntok = ntok;
-  }
-  // ring stages: as many as fit next to the barriers (and, gated epilogues, the residual tile);
-  // the transposed accumulator tile reuses the ring. >= 80 KB: at most 2 CTAs (2 x 256 TMEM columns)
-  // per SM, so no TMEM allocation waits
-  const int stage_bytes = A_BYTES + ntok * BK * 2, slack = 1024 + 256, res_bytes = ntok * BM * 2;
-  int stage_n[2], smem_n[2];
-  for (int r = 0; r < 2; ++r) {
-    const int extra = r ? res_bytes : 0;
-    int st = (SMEM_BUDGET - slack - extra) / stage_bytes;
-    if (st > MAX_STAGES) st = MAX_STAGES;
-    if (((ntok + 31) / 32) * 32 * TS * 4 > st * stage_bytes) return MKX_ERR_UNSUPPORTED;  // transposed tile fits
-    stage_n[r] = st;
-    smem_n[r] = st * stage_bytes + slack + extra;
-    if (smem_n[r] < 80 * 1024) smem_n[r] = 80 * 1024;
-  }
   const int MODW = 9 * L * H + 2 * H;
   const long long ep_stride = (long long)(in->n_steps + 1) * MODW;
   const long long kvm_ep = (long long)L * in->mem_rows * H, kvc_ep = (long long)L * in->ca_rows * H;
   const float scale = 1.0f / sqrtf((float)HD);
-  const size_t att_sa = (size_t)(16 + 2 * SA_MAXK) * KS * 2;
+  const int kcap = (in->mem_rows + T + CA_BLK - 1) / CA_BLK * CA_BLK;  // <= SA_MAXK
+  const size_t att_sa = (size_t)(16 + 2 * kcap) * KS * 2;
   const size_t att_ca = (size_t)(16 + 4 * CA_BLK) * KS * 2;
   cudaError_t err = cudaSuccess;
-  auto gemm = [&](int g, int l, const CUtensorMap& map, uint16_t* out, int ldo, const uint16_t* gate) {
-    if (err != cudaSuccess) return;
+  mkx_status st = MKX_OK;
+  auto gemm = [&](int g, int l, int buf, uint16_t* out, int ldo, const uint16_t* gate) {
+    if (err != cudaSuccess || st != MKX_OK) return;
     const GemmShape s = gemm_shape(g, I);
+    const int ntok = gemm_token_tile(M, s.ntiles, h->sms), ttiles = (M + ntok - 1) / ntok;
+    const CUtensorMap* map = token_map(h, buf, ntok);
+    GemmLaunch gl;
+    if (!map || !gemm_launch_shape(ntok, g != G_D && s.epi == E_GATED, &gl)) {
+      st = map ? MKX_ERR_UNSUPPORTED : MKX_ERR_CUDA;
+      return;
+    }
     GemmParams p;
     memset(&p, 0, sizeof(p));
     p.wpk = h->wpk[g] + (size_t)l * s.ntiles * s.ktiles * (A_BYTES / 2);
@@ -978,8 +1002,11 @@ extern "C" mkx_status mkx_batch_run(mkx_batch_handle* h, const mkx_batch_inputs*
     p.M = M;
     p.T = T;
     p.epi = p.splits > 1 ? E_PARTIAL : s.epi;
-    const int rg = p.epi == E_GATED ? 1 : 0;
-    p.stages = stage_n[rg];
+    if (p.epi != E_GATED && !gemm_launch_shape(ntok, false, &gl)) {
+      st = MKX_ERR_UNSUPPORTED;
+      return;
+    }
+    p.stages = gl.stages;
     p.out = out;
     p.ldo = ldo;
     p.ws = h->ws;
@@ -988,7 +1015,7 @@ extern "C" mkx_status mkx_batch_run(mkx_batch_handle* h, const mkx_batch_inputs*
     p.gate_stride = ep_stride;
     p.status = h->status;
     p.timeout_ns = h->timeout_ns;
-    err = launch_pdl(bt_gemm, dim3(s.ntiles, ttiles, p.splits), dim3(GEMM_THREADS), (size_t)smem_n[rg], stream, map, p);
+    err = launch_pdl(bt_gemm, dim3(s.ntiles, ttiles, p.splits), dim3(GEMM_THREADS), (size_t)gl.smem, stream, *map, p);
     if (err == cudaSuccess && p.splits > 1)
       err = launch_pdl(bt_reduce_gated, dim3((M * (H / 2) + 255) / 256), dim3(256), 0, stream, (const float*)h->ws,
                        p.splits, Mp, M, T, out, gate, ep_stride);
@@ -1035,7 +1062,7 @@ extern "C" mkx_status mkx_batch_run(mkx_batch_handle* h, const mkx_batch_inputs*
       ap.scale = scale;
       // self-attention block
       adarms(blk);
-      gemm(G_QKV, l, h->map_a, h->qkv, 3 * H, nullptr);
+      gemm(G_QKV, l, 0, h->qkv, 3 * H, nullptr);
       ap.src = h->qkv;
       ap.src_ld = 3 * H;
       ap.kb = in->memk + (size_t)l * in->mem_rows * H;
@@ -1047,12 +1074,13 @@ extern "C" mkx_status mkx_batch_run(mkx_batch_handle* h, const mkx_batch_inputs*
       ap.sin = in->sa_sin;
       ap.wq = h->nrm + (size_t)l * HD;
       ap.wk = h->nrm + (size_t)(L + l) * HD;
+      ap.kcap = kcap;
       if (err == cudaSuccess)
         err = launch_pdl(bt_attention<true>, dim3(B * NH), dim3(32 * ATT_WARPS), att_sa, stream, ap);
-      gemm(G_O, l, h->map_y, h->h, H, blk + 2 * H);
+      gemm(G_O, l, 1, h->h, H, blk + 2 * H);
       // cross-attention block
       adarms(blk + 3 * H);
-      gemm(G_CAQ, l, h->map_a, h->qkv, H, nullptr);  // the query in the qkv buffer, rows of H
+      gemm(G_CAQ, l, 0, h->qkv, H, nullptr);  // the query in the qkv buffer, rows of H
       ap.src = h->qkv;
       ap.src_ld = H;
       ap.kb = in->kca + (size_t)l * in->ca_rows * H;
@@ -1066,15 +1094,19 @@ extern "C" mkx_status mkx_batch_run(mkx_batch_handle* h, const mkx_batch_inputs*
       ap.wk = nullptr;
       if (err == cudaSuccess)
         err = launch_pdl(bt_attention<false>, dim3(B * NH), dim3(32 * ATT_WARPS), att_ca, stream, ap);
-      gemm(G_OCA, l, h->map_y, h->h, H, blk + 5 * H);
+      gemm(G_OCA, l, 1, h->h, H, blk + 5 * H);
       // MLP block
       adarms(blk + 6 * H);
-      gemm(G_GU, l, h->map_a, h->g, I, nullptr);
-      gemm(G_D, l, h->map_g, h->h, H, blk + 8 * H);
+      gemm(G_GU, l, 0, h->g, I, nullptr);
+      gemm(G_D, l, 2, h->h, H, blk + 8 * H);
     }
     tail(0, s + 1 == in->n_steps, s);
   }
   if (err != cudaSuccess) return batch_fail(err, "mkx_batch_run launch");
+  if (st != MKX_OK) {
+    snprintf(g_batch_err, sizeof(g_batch_err), "mkx_batch_run: tensor map or launch shape");
+    return st;
+  }
   return MKX_OK;
 }
 

@@ -42,7 +42,7 @@ def _c_layout(struct: str, fields):
     if not gcc:
         pytest.skip("gcc missing")
     body = "".join(f'printf("{f} %zu\\n", offsetof({struct}, {f}));' for f in fields)
-    src = f'#include <stdio.h>\n#include <stddef.h>\n#include "mkx.h"\n#include "mkx_prepare.h"\nint main(void){{{body} printf("sizeof %zu\\n", sizeof({struct})); return 0;}}\n'
+    src = f'#include <stdio.h>\n#include <stddef.h>\n#include "mkx.h"\n#include "mkx_prepare.h"\n#include "mkx_batch.h"\nint main(void){{{body} printf("sizeof %zu\\n", sizeof({struct})); return 0;}}\n'
     import tempfile
     from pathlib import Path
     with tempfile.TemporaryDirectory() as d:
@@ -57,7 +57,8 @@ def _c_layout(struct: str, fields):
 
 
 @pytest.mark.parametrize("struct,cls", [("mkx_dims", "Dims"), ("mkx_weights", "Weights"), ("mkx_step_inputs", "StepInputs"),
-                                        ("mkx_packed_weights", "PackedWeights"), ("mkx_prep_dims", "PrepDims")])
+                                        ("mkx_packed_weights", "PackedWeights"), ("mkx_prep_dims", "PrepDims"),
+                                        ("mkx_batch_inputs", "BatchInputs")])
 def test_struct_layout_matches_c(struct, cls):
     from reki_megakernel_b200 import _lib
     ct = getattr(_lib, cls)
@@ -97,6 +98,23 @@ def test_static_entry_rejects_a_misaligned_error_word_without_a_device():
     si.T = 10
     assert lib.mkx_run_static(C.byref(d), C.byref(pw), C.byref(si), C.c_void_p(0x1002), None) == _lib.MKX_ERR_INVALID_ARG
     assert b"aligned" in lib.mkx_last_cuda_error()
+
+
+def test_batch_arguments_are_rejected_without_a_device():
+    from reki_megakernel_b200 import _lib
+    lib = _lib.load()
+    h = C.c_void_p()
+    assert lib.mkx_batch_create(None, None, 8, 0, C.byref(h)) == _lib.MKX_ERR_INVALID_ARG
+    d = _lib.Dims(L=10, H=768, NH=12, HD=64, I=3072, A=32, eps=1e-6, qk_eps=1e-6, max_rows=16, grid=0)
+    w = _lib.Weights(*([1] * 14))
+    assert lib.mkx_batch_create(C.byref(d), C.byref(w), 0, 0, C.byref(h)) == _lib.MKX_ERR_INVALID_ARG  # no episodes
+    d.I = 1000                                                                     # not a multiple of 128
+    assert lib.mkx_batch_create(C.byref(d), C.byref(w), 8, 0, C.byref(h)) == _lib.MKX_ERR_UNSUPPORTED
+    assert lib.mkx_batch_run(None, None, None) == _lib.MKX_ERR_INVALID_ARG
+    assert lib.mkx_batch_launches(None, 8, 10, 9) == -1
+    assert lib.mkx_batch_last_error(None, None) == _lib.MKX_ERR_INVALID_ARG
+    assert lib.mkx_batch_copy_state(None, 0, None, 0) == _lib.MKX_ERR_INVALID_ARG
+    lib.mkx_batch_destroy(None)
 
 
 def test_prepare_arguments_are_rejected_without_a_device():
