@@ -371,6 +371,76 @@ def run_predict(args):
     print(json.dumps(line), flush=True)
 
 
+def run_full(args):
+    """A whole predict: all 10 Euler steps in one persistent launch, the step
+    modulations, register_prepare, the register pass of the current frame and the carry of 3 register
+    frames x 32 rows, as one CUDA graph (FullPredict), over consecutive seeded predicts. Prints one
+    JSON line (not the headline metric)."""
+    from reki_megakernel_b200.batch import BatchedExpert
+    from reki_megakernel_b200.full_predict import FullPredict
+    from reki_megakernel_b200.mk_expert import ExpertMegakernel
+    from reki_megakernel_b200.modulations import StepModulations
+    from reki_megakernel_b200.prepare import RegisterPrepare
+    from reki_megakernel_b200.synthetic import (ExpertDims, make_modulation_weights, make_prepare_weights,
+                                                make_register_rows, make_source, make_state, make_weights)
+    dims = ExpertDims()
+    S, R, N, T = args.S, 32, 10, 10
+    w = make_weights(dims, seed=0).to("cuda")
+    mk = ExpertMegakernel(weights=w)
+    bx = BatchedExpert(w, max_episodes=R // 16)
+    rp = RegisterPrepare(make_prepare_weights(dims, seed=0).to("cuda"))
+    sm = StepModulations(make_modulation_weights(dims, seed=0).to("cuda"))
+    fp = FullPredict(mk, bx, rp, sm, make_register_rows(dims, R).to("cuda"), S=S, num_steps=N, T=T)
+    n_in = 20  # 20 consecutive seeded predicts, repeated
+    ins = [(make_source(S, dims.src_dim, seed=100 + p).to("cuda"), make_state(sm.sdim, seed=100 + p).to("cuda"),
+            torch.randn((1, T, dims.A), generator=torch.Generator().manual_seed(1234 + p)).to("cuda"))
+           for p in range(n_in)]
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    for i in range(args.warmup):
+        fp(*ins[i % n_in])
+    torch.cuda.synchronize()
+    fp.check_device_errors()
+    fp.reset()
+    clocks = Clocks(0)
+    clocks.start()
+    time.sleep(0.3)
+    per = []
+    for i in range(args.steps):
+        flush.fill_(1)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fp(*ins[i % n_in])
+        b.record()
+        b.synchronize()
+        per.append(a.elapsed_time(b))
+    clk = clocks.stop()
+    fp.check_device_errors()
+    L, H, I = dims.L, dims.H, dims.I
+    layer_w = L * (3 * H * H + 3 * H * H + 3 * I * H) * 2
+    reg_launches = bx.launches(R // 16, 16, 1) - 2 + L  # the pass: per layer the loop's launches plus the frame write
+    wbytes = (N * algorithmic_bytes_per_step(dims, dims.MODW * 2) + layer_w + dims.MODW * H * 2 + dims.MODW * 4
+              + L * 2 * H * dims.src_dim * 2)
+    ms = statistics.mean(per)
+    hbm, peak_kind = peaks()
+    achieved = wbytes / (ms * 1e-3) / 1e9
+    line = {
+        "metric": "whole predict: 10 Euler steps + modulations + register_prepare + register pass + frame carry, ms",
+        "value": ms, "unit": "ms", "higher_is_better": False, "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "dtype": "bf16", "data": "synthetic (seeded weights; 20 seeded predicts repeated)",
+        "ms_p50": statistics.median(per), "ms_p99": sorted(per)[min(len(per) - 1, int(0.99 * len(per)))],
+        "config": {"workload": f"BASELINE configs[2]: one CUDA graph per predict; S={S} source rows x 2048, "
+                               f"{R} register rows per frame, 3 frames carried, T={T} action rows, N={N} steps "
+                               "in one persistent launch",
+                   "S": S, "T": T, "euler_steps": N, "register_rows": R, "frames": 3,
+                   "l2": "256 MB written between timed predicts (untimed)"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_kind": f"{peak_kind} (hbm copy, burst)", "algorithmic_bytes": wbytes},
+        "gpu_launches": (4 + reg_launches) * args.steps,
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_mods(args):
     """Per-step modulation rows of one predict (BASELINE configs[2]'s modulation part): N = 10 rows of
     MODW = 70,656 from the conditioning network, two launches (conditioning + HBM-bound projection).
@@ -844,15 +914,17 @@ def main():
     ap.add_argument("--mods", action="store_true", help="time the per-step modulation rows (_step_modulations), own JSON line")
     ap.add_argument("--predict", action="store_true",
                     help="time the GPU half of a predict after step 1 (modulations + K/V preparation + expert) as one graph")
+    ap.add_argument("--full", action="store_true",
+                    help="time whole carried predicts (all 10 steps, register pass, frame carry) as one graph each")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    if args.timeline or args.substage or args.prepare or args.mods or args.predict:
+    if args.timeline or args.substage or args.prepare or args.mods or args.predict or args.full:
         if rank == 0:
             (run_timeline if args.timeline else run_substage if args.substage else run_prepare if args.prepare
-             else run_mods if args.mods else run_predict)(args)
+             else run_mods if args.mods else run_full if args.full else run_predict)(args)
         return
     if world > 1:
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")

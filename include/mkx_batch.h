@@ -63,6 +63,37 @@ mkx_status mkx_batch_create(const mkx_dims* dims, const mkx_weights* w, int max_
  * synchronisation, capturable in a CUDA graph. One run in flight per handle. */
 mkx_status mkx_batch_run(mkx_batch_handle* h, const mkx_batch_inputs* in, cudaStream_t stream);
 
+/* Inputs of the register pass: the R register rows of the current frame through every layer of the
+ * expert with plain norms (no modulation: AdaRMS scale and shift 0, residual gates 1), each layer
+ * first writing the rows' own K (per-head RMSNorm with 1 + k_norm, RoPE) and V into the memory rows
+ * [mem_rows - R, mem_rows), then attending over the memory rows [kv_start, mem_rows) -- the older
+ * frames and the current one -- and over the cross-attention source. Restates the register half of
+ * Kyutai's Euler step 1 (`_expert_first_step`, bound at src/mk_expert.py:527-533, described in the
+ * reference README: register rows with plain norms, attention over the register buffer, the register
+ * K/V as output); that function is absent from the reference checkout, so the restatement is not
+ * pinned to it. One memory and one source for all R rows (one episode). */
+typedef struct {
+  const uint16_t* reg_in;   /* [R, H] bf16 register rows entering layer 0 */
+  uint16_t* memk;           /* [L, PM, NH, HD] bf16 register memory K: rows [PM - R, PM) written */
+  uint16_t* memv;
+  const int* kv_start;      /* [1] int32 first valid memory row (<= PM - R) */
+  int mem_rows;             /* PM, R <= PM <= 256 */
+  const uint16_t* kca;      /* [L, SP, NH, HD] bf16 cross-attention K (rows < src_rows valid) */
+  const uint16_t* vca;
+  const int* src_rows;      /* [1] int32, 1 <= S <= SP */
+  int ca_rows;              /* SP <= 4096 */
+  const float* sa_cos;      /* [R, HD] fp32 RoPE tables of the register rows (self-attention) */
+  const float* sa_sin;
+  const float* ca_cos;      /* [R, HD] fp32 (cross-attention) */
+  const float* ca_sin;
+  int R;                    /* register rows: a multiple of 16, <= 16 * max_episodes */
+} mkx_register_inputs;
+
+/* Enqueues the register pass on `stream` (12 or 13 launches per layer, programmatic dependents, no
+ * host synchronisation, capturable). Uses the handle's activation buffers: not concurrent with
+ * mkx_batch_run on the same handle. */
+mkx_status mkx_batch_register_pass(mkx_batch_handle* h, const mkx_register_inputs* in, cudaStream_t stream);
+
 /* Reads the device error word (synchronous): 0 when every bounded wait completed. */
 mkx_status mkx_batch_last_error(mkx_batch_handle* h, int* code);
 

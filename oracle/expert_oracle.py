@@ -83,9 +83,10 @@ class OracleExpert:
         return self._r(xn * cos + sign * xpn * sin)
 
     # ---- attention ---------------------------------------------------------------------------
-    def _sa(self, l, qkv, memk, memv, kv_start, cos, sin):
+    def _sa(self, l, qkv, memk, memv, kv_start, cos, sin, own: bool = True):
         """Self-attention of the action rows over [memory rows kv_start..PM || own rows]
-        (``src/mk_expert.py:196-222``)."""
+        (``src/mk_expert.py:196-222``); ``own=False``: the memory rows only (the register pass, whose
+        rows are already in the memory)."""
         d = self.d
         H, NH, HD = d.H, d.NH, d.HD
         scale = HD ** -0.5
@@ -98,10 +99,13 @@ class OracleExpert:
             v = qkv[:, 2 * H + h * HD: 2 * H + (h + 1) * HD]
             mk = memk[l, kv_start:, h].float()
             mv = memv[l, kv_start:, h].float()
+            if not own:
+                k, v = k[:0], v[:0]
             s1 = (q @ mk.T) * scale
             s2 = (q @ k.T) * scale
-            mx = torch.maximum(s1.amax(1, keepdim=True) if s1.shape[1] else torch.full((T, 1), -float("inf"), device=q.device),
-                               s2.amax(1, keepdim=True))
+            ninf = torch.full((T, 1), -float("inf"), device=q.device)
+            mx = torch.maximum(s1.amax(1, keepdim=True) if s1.shape[1] else ninf,
+                               s2.amax(1, keepdim=True) if s2.shape[1] else ninf)
             p1 = torch.exp(s1 - mx)
             p2 = torch.exp(s2 - mx)
             den = p1.sum(1, keepdim=True) + p2.sum(1, keepdim=True)
@@ -144,16 +148,28 @@ class OracleExpert:
         return y
 
     # ---- one episode ---------------------------------------------------------------------------
-    def layer(self, l, h, mrow, ep):
-        """One expert layer (8 stages of ``src/mk_expert.py:342-421``). Returns (h_out, parts)."""
+    def layer(self, l, h, mrow, ep, frame_row0: int | None = None):
+        """One expert layer (8 stages of ``src/mk_expert.py:342-421``). Returns (h_out, parts).
+
+        ``frame_row0`` set: the register pass -- the rows' own K (norm + RoPE, rounded) and V are first
+        written into ``ep["memk"]`` / ``ep["memv"]`` rows [frame_row0, frame_row0 + rows) of layer l,
+        then the self-attention reads the memory rows only."""
         d = self.d
-        H = d.H
+        H, NH, HD = d.H, d.NH, d.HD
         m_sa = mrow[(3 * l) * 3 * H:]
         m_ca = m_sa[3 * H:]
         m_mlp = m_ca[3 * H:]
         a = self._adarms(h, m_sa[:H], m_sa[H:2 * H])
         qkv = self._linear(a, self.wqkv[l])
-        y = self._sa(l, qkv, ep["memk"], ep["memv"], ep["kv_start"], ep["sa_cos"], ep["sa_sin"])
+        if frame_row0 is not None:
+            R = qkv.shape[0]
+            for hh in range(NH):
+                k = self._norm_rope(qkv[:, H + hh * HD: H + (hh + 1) * HD], self.kn[l], ep["sa_cos"], ep["sa_sin"])
+                ep["memk"][l, frame_row0:frame_row0 + R, hh] = k.to(ep["memk"].dtype)
+                ep["memv"][l, frame_row0:frame_row0 + R, hh] = qkv[:, 2 * H + hh * HD: 2 * H + (hh + 1) * HD].to(
+                    ep["memv"].dtype)
+        y = self._sa(l, qkv, ep["memk"], ep["memv"], ep["kv_start"], ep["sa_cos"], ep["sa_sin"],
+                     own=frame_row0 is None)
         h2 = self._gated(h, y @ self.wo[l].T, m_sa[2 * H:3 * H])
         a = self._adarms(h2, m_ca[:H], m_ca[H:2 * H])
         qca = self._linear(a, self.wqca[l])

@@ -53,6 +53,12 @@ class BatchInputs(C.Structure):
                 ("n_steps", C.c_int), ("action_dim", C.c_int)]
 
 
+class RegisterInputs(C.Structure):
+    _fields_ = [("reg_in", P), ("memk", P), ("memv", P), ("kv_start", P), ("mem_rows", C.c_int), ("kca", P),
+                ("vca", P), ("src_rows", P), ("ca_rows", C.c_int), ("sa_cos", P), ("sa_sin", P), ("ca_cos", P),
+                ("ca_sin", P), ("R", C.c_int)]
+
+
 class PrepDims(C.Structure):
     _fields_ = [("L", C.c_int), ("H", C.c_int), ("NH", C.c_int), ("HD", C.c_int), ("src_dim", C.c_int),
                 ("eps", C.c_float)]
@@ -78,6 +84,7 @@ SIGNATURES = {
     "mkx_destroy": (None, [P]),
     "mkx_batch_create": (C.c_int, [C.POINTER(Dims), C.POINTER(Weights), C.c_int, C.c_int, C.POINTER(P)]),
     "mkx_batch_run": (C.c_int, [P, C.POINTER(BatchInputs), P]),
+    "mkx_batch_register_pass": (C.c_int, [P, C.POINTER(RegisterInputs), P]),
     "mkx_batch_last_error": (C.c_int, [P, C.POINTER(C.c_int)]),
     "mkx_batch_launches": (C.c_int, [P, C.c_int, C.c_int, C.c_int]),
     "mkx_batch_last_cuda_error": (C.c_char_p, []),

@@ -116,6 +116,50 @@ class BatchedExpert:
         self._keep = ts  # converted tensors stay alive until the next call
         return out
 
+    def register_pass(self, reg_in: torch.Tensor, memk: torch.Tensor, memv: torch.Tensor, kv_start: torch.Tensor,
+                      kca: torch.Tensor, vca: torch.Tensor, src_rows: torch.Tensor, sa_pe, ca_pe) -> None:
+        """The current frame's R register rows through every layer with plain norms
+        (``include/mkx_batch.h``, ``mkx_batch_register_pass``): writes each layer's register K / V
+        into memory rows [PM - R, PM) of ``memk`` / ``memv`` [L, PM, NH, HD] bf16 (in place), the
+        self-attention reading rows [kv_start, PM). ``reg_in`` [R, H] bf16 (R a multiple of 16);
+        ``kca`` / ``vca`` [L, SP, NH, HD] bf16 valid below ``src_rows``; ``kv_start`` and ``src_rows``
+        one-element int32 device tensors; ``sa_pe`` / ``ca_pe`` (cos, sin) fp32 [R, HD]. Asynchronous
+        on the current stream, graph-capturable; shares the handle's buffers with ``run``."""
+        d = self.dims
+        if reg_in.dim() != 2 or reg_in.shape[1] != d.H or reg_in.dtype != torch.bfloat16:
+            raise ValueError(f"reg_in must be bf16 [R, {d.H}]")
+        R = reg_in.shape[0]
+        if R < 16 or R % 16 or R > 16 * self.max_episodes:
+            raise ValueError(f"R={R} must be a multiple of 16 in 16..{16 * self.max_episodes}")
+        PM, SP = memk.shape[1], kca.shape[1]
+        for k, v, shp in (("memk", memk, (d.L, PM, d.NH, d.HD)), ("memv", memv, (d.L, PM, d.NH, d.HD)),
+                          ("kca", kca, (d.L, SP, d.NH, d.HD)), ("vca", vca, (d.L, SP, d.NH, d.HD))):
+            if tuple(v.shape) != shp or v.dtype != torch.bfloat16:
+                raise ValueError(f"{k} must be bf16 {list(shp)}")
+        if PM < R:
+            raise ValueError(f"the memory ({PM} rows) must hold the frame's {R} rows")
+        tabs = [*sa_pe, *ca_pe]
+        for t in tabs:
+            if tuple(t.shape) != (R, d.HD) or t.dtype != torch.float32:
+                raise ValueError(f"RoPE tables must be fp32 [{R}, {d.HD}]")
+        ints = (kv_start, src_rows)
+        for t in ints:
+            if t.dtype != torch.int32 or t.numel() < 1:
+                raise ValueError("kv_start and src_rows must be int32 device tensors")
+        for t in (reg_in, memk, memv, kca, vca, *tabs, *ints):
+            if t.device != self.device:
+                raise ValueError(f"every tensor must be on the expert's device {self.device}")
+            if not t.is_contiguous():
+                raise ValueError("every tensor must be contiguous")
+        ri = _lib.RegisterInputs(
+            reg_in=reg_in.data_ptr(), memk=memk.data_ptr(), memv=memv.data_ptr(), kv_start=kv_start.data_ptr(),
+            mem_rows=PM, kca=kca.data_ptr(), vca=vca.data_ptr(), src_rows=src_rows.data_ptr(), ca_rows=SP,
+            sa_cos=tabs[0].data_ptr(), sa_sin=tabs[1].data_ptr(), ca_cos=tabs[2].data_ptr(), ca_sin=tabs[3].data_ptr(),
+            R=R)
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        _lib.check(self._lib.mkx_batch_register_pass(self._h, C.byref(ri), C.c_void_p(stream)),
+                   "mkx_batch_register_pass")
+
     STATE = {"h": 0, "a": 1, "qkv": 2, "y": 3, "g": 4, "x": 5}
 
     def state(self, name: str, rows: int, cols: int) -> torch.Tensor:

@@ -411,6 +411,8 @@ struct AttnParams {
   const float* wk;       // [HD] 1 + k norm weight (SA own keys)
   int T;
   int kcap;              // SA: key rows of the shared K / V tiles (PM + T rounded up to 64)
+  int own;               // SA: 1 the query rows' own keys follow the memory rows; 0 memory rows only
+  int lim_stride;        // episode stride of lim (0: one value for all episodes)
   float qk_eps, scale;
 };
 
@@ -447,13 +449,13 @@ __global__ void __launch_bounds__(32 * ATT_WARPS) bt_attention(const __grid_cons
   };
   int nm = 0, nk = 0, S = 0;
   if (SA) {
-    const int k0 = min(max(p.lim[e], 0), p.kv_rows);
+    const int k0 = min(max(p.lim[e * p.lim_stride], 0), p.kv_rows);
     nm = p.kv_rows - k0;
-    nk = nm + T;
+    nk = nm + (p.own ? T : 0);
     stage(k0, nm, 0, tid, 32 * ATT_WARPS);
     zero_rows(nk, (nk + CA_BLK - 1) / CA_BLK * CA_BLK, tid, 32 * ATT_WARPS);
   } else {
-    S = min(max(p.lim[e], 1), p.kv_rows);
+    S = min(max(p.lim[e * p.lim_stride], 1), p.kv_rows);
     const int nb = min(CA_BLK, S);
     stage(0, nb, 0, tid, 32 * ATT_WARPS);
     zero_rows(nb, CA_BLK, tid, 32 * ATT_WARPS);
@@ -471,7 +473,7 @@ __global__ void __launch_bounds__(32 * ATT_WARPS) bt_attention(const __grid_cons
       const float2 q = norm_rope_row(bf_lo(u), bf_hi(u), *reinterpret_cast<const float2*>(p.wq + 2 * lane), cs, sn,
                                      p.qk_eps, lane);
       qv = pack_bf2(q.x, q.y);
-      if (SA) {
+      if (SA && p.own) {
         u = *reinterpret_cast<const uint32_t*>(row + H + 2 * lane);
         const float2 k = norm_rope_row(bf_lo(u), bf_hi(u), *reinterpret_cast<const float2*>(p.wk + 2 * lane), cs, sn,
                                        p.qk_eps, lane);
@@ -618,6 +620,28 @@ __global__ void __launch_bounds__(32 * ATT_WARPS) bt_attention(const __grid_cons
       *reinterpret_cast<uint32_t*>(p.y + ((size_t)e * T + g + 8) * H + h * HD + d) =
           pack_bf2(o[dn][2] / den1, o[dn][3] / den1);
   }
+}
+
+// The register pass's own K (per-head RMSNorm with 1 + k_norm, then RoPE at the rows' positions, a bf16
+// rounding after each, as every key the self-attention reads) and V of one layer, written into the
+// memory rows [row0, row0 + R) of that layer before its self-attention reads the memory: one warp per
+// (row, head).
+__global__ void __launch_bounds__(256) bt_write_frame(const uint16_t* __restrict__ qkv, int R, uint16_t* mk, uint16_t* mv,
+                                                      int row0, const float* __restrict__ wk, const float* __restrict__ cos,
+                                                      const float* __restrict__ sin, float eps) {
+  grid_dep_wait();
+  if (threadIdx.x == 0) grid_dep_launch();
+  const int w = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (w >= R * NH) return;  // whole warps
+  const int r = w / NH, hh = w % NH;
+  const uint16_t* row = qkv + (size_t)r * 3 * H + hh * HD + 2 * lane;
+  const uint32_t u = *reinterpret_cast<const uint32_t*>(row + H);
+  const float2 k = norm_rope_row(bf_lo(u), bf_hi(u), *reinterpret_cast<const float2*>(wk + 2 * lane),
+                                 *reinterpret_cast<const float2*>(cos + (size_t)r * HD + 2 * lane),
+                                 *reinterpret_cast<const float2*>(sin + (size_t)r * HD + 2 * lane), eps, lane);
+  *reinterpret_cast<uint32_t*>(mk + (size_t)(row0 + r) * H + hh * HD + 2 * lane) = pack_bf2(k.x, k.y);
+  *reinterpret_cast<uint32_t*>(mv + (size_t)(row0 + r) * H + hh * HD + 2 * lane) =
+      *reinterpret_cast<const uint32_t*>(row + 2 * H);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -767,6 +791,7 @@ struct mkx_batch_handle {
   int device, max_ep, Mp_max, sms;
   uint16_t* wpk[NGEMM];  // per GEMM: [L][tiles][ktiles] blocks
   float* nrm;            // [3][L][HD] 1 + norm weights
+  uint16_t* plain;       // one modulation row [MODW] bf16: scale = shift = 0, gates 1 (register rows)
   float *win, *bin, *wout, *bout;
   uint16_t *h, *a, *qkv, *y, *g;
   float* xs;
@@ -820,6 +845,7 @@ extern "C" mkx_status mkx_batch_create(const mkx_dims* dims, const mkx_weights* 
     alloc((void**)&h->wpk[g], (size_t)L * s.ntiles * s.ktiles * A_BYTES);
   }
   alloc((void**)&h->nrm, (size_t)3 * L * HD * 4);
+  alloc((void**)&h->plain, (size_t)(9 * L * H + 2 * H) * 2);
   alloc((void**)&h->win, (size_t)A * H * 4);
   alloc((void**)&h->bin, (size_t)H * 4);
   alloc((void**)&h->wout, (size_t)A * H * 4);
@@ -848,6 +874,19 @@ extern "C" mkx_status mkx_batch_create(const mkx_dims* dims, const mkx_weights* 
     }
   }
   bt_norm_kernel<<<(3 * L * HD + 255) / 256, 256>>>(w->qn, w->kn, w->qcan, h->nrm, L);
+  {
+    const int MODW = 9 * L * H + 2 * H;
+    uint16_t* pl = new (std::nothrow) uint16_t[MODW];
+    if (!pl) ok = false;
+    if (ok) {
+      for (int i = 0; i < MODW; ++i) {
+        const int within = i < 9 * L * H ? (i % (3 * H)) / H : 0;  // 0 scale, 1 shift, 2 gate
+        pl[i] = within == 2 ? (uint16_t)0x3F80 : (uint16_t)0;       // bf16 1.0 / 0.0
+      }
+      cudaMemcpy(h->plain, pl, (size_t)MODW * 2, cudaMemcpyHostToDevice);
+    }
+    delete[] pl;
+  }
   cudaMemcpy(h->win, w->win, (size_t)A * H * 4, cudaMemcpyDeviceToDevice);
   cudaMemcpy(h->bin, w->bin, (size_t)H * 4, cudaMemcpyDeviceToDevice);
   cudaMemcpy(h->wout, w->wout, (size_t)A * H * 4, cudaMemcpyDeviceToDevice);
@@ -862,7 +901,8 @@ extern "C" mkx_status mkx_batch_create(const mkx_dims* dims, const mkx_weights* 
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e == cudaSuccess) e = cudaFuncSetAttribute(bt_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BUDGET);
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(bt_attention<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+    e = cudaFuncSetAttribute(bt_attention<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (16 + 2 * SA_MAXK) * KS * 2);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(bt_attention<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
   if (e != cudaSuccess) {
@@ -951,6 +991,154 @@ const CUtensorMap* token_map(mkx_batch_handle* h, int buf, int ntok) {
 }
 }  // namespace
 
+namespace {
+// One enqueue sequence: the launches of a run share these.
+struct Seq {
+  mkx_batch_handle* h;
+  cudaStream_t stream;
+  int B, T, M, Mp;
+  long long ep_stride;  // episode stride of the modulation rows (0: one row for every episode)
+  cudaError_t err;
+  mkx_status st;
+};
+
+void seq_gemm(Seq& q, int g, int l, int buf, uint16_t* out, int ldo, const uint16_t* gate) {
+  if (q.err != cudaSuccess || q.st != MKX_OK) return;
+  mkx_batch_handle* h = q.h;
+  const GemmShape s = gemm_shape(g, h->d.I);
+  const int ntok = gemm_token_tile(q.M, s.ntiles, h->sms), ttiles = (q.M + ntok - 1) / ntok;
+  const CUtensorMap* map = token_map(h, buf, ntok);
+  GemmParams p;
+  memset(&p, 0, sizeof(p));
+  p.splits = g == G_D ? down_splits(s, ttiles, h->sms) : 1;
+  p.kps = (s.ktiles + p.splits - 1) / p.splits;
+  p.splits = (s.ktiles + p.kps - 1) / p.kps;
+  p.epi = p.splits > 1 ? E_PARTIAL : s.epi;
+  GemmLaunch gl;
+  if (!map || !gemm_launch_shape(ntok, p.epi == E_GATED, &gl)) {
+    q.st = map ? MKX_ERR_UNSUPPORTED : MKX_ERR_CUDA;
+    return;
+  }
+  p.wpk = h->wpk[g] + (size_t)l * s.ntiles * s.ktiles * (A_BYTES / 2);
+  p.ktiles = s.ktiles;
+  p.ntok = ntok;
+  p.M = q.M;
+  p.T = q.T;
+  p.stages = gl.stages;
+  p.out = out;
+  p.ldo = ldo;
+  p.ws = h->ws;
+  p.Mp = q.Mp;
+  p.gate = gate;
+  p.gate_stride = q.ep_stride;
+  p.status = h->status;
+  p.timeout_ns = h->timeout_ns;
+  q.err = launch_pdl(bt_gemm, dim3(s.ntiles, ttiles, p.splits), dim3(GEMM_THREADS), (size_t)gl.smem, q.stream, *map, p);
+  if (q.err == cudaSuccess && p.splits > 1)
+    q.err = launch_pdl(bt_reduce_gated, dim3((q.M * (H / 2) + 255) / 256), dim3(256), 0, q.stream, (const float*)h->ws,
+                       p.splits, q.Mp, q.M, q.T, out, gate, q.ep_stride);
+}
+
+void seq_adarms(Seq& q, const uint16_t* blk) {
+  if (q.err != cudaSuccess) return;
+  q.err = launch_pdl(bt_adarms, dim3((q.Mp + 7) / 8), dim3(256), 0, q.stream, (const uint16_t*)q.h->h, q.h->a, q.M, q.Mp,
+                     q.T, blk, q.ep_stride, q.h->d.eps);
+}
+
+// What one layer reads besides the handle's buffers: the episodes' register memory and
+// cross-attention K/V of this layer (episode strides kvm_ep / kvc_ep; 0 = shared by all), their row
+// limits (lim_stride 0 = one value for all), the RoPE tables of the query rows, and -- register pass
+// only -- the memory rows [frame_row0, frame_row0 + M) where the rows' own K / V go before the
+// self-attention reads the memory (own = 0: no own-row keys besides).
+struct LayerIO {
+  const uint16_t* memk;
+  const uint16_t* memv;
+  long long kvm_ep;
+  int mem_rows;
+  const int* kv_start;
+  const uint16_t* kca;
+  const uint16_t* vca;
+  long long kvc_ep;
+  int ca_rows;
+  const int* src_rows;
+  int lim_stride, own;
+  const float *sa_cos, *sa_sin, *ca_cos, *ca_sin;
+  int frame_row0;  // < 0: no frame to write
+};
+
+// The 11-12 launches of one layer (src/mk_expert.py:342-421); blk: this layer's modulation blocks
+// [SA | CA | MLP] x [scale, shift, gate] of episode 0.
+void seq_layer(Seq& q, int l, const uint16_t* blk, const LayerIO& io) {
+  mkx_batch_handle* h = q.h;
+  const int L = h->d.L, I = h->d.I;
+  const int kcap = (io.mem_rows + (io.own ? q.T : 0) + CA_BLK - 1) / CA_BLK * CA_BLK;  // <= SA_MAXK
+  const size_t att_sa = (size_t)(16 + 2 * kcap) * KS * 2;
+  const size_t att_ca = (size_t)(16 + 4 * CA_BLK) * KS * 2;
+  const uint16_t* memk_l = io.memk + (size_t)l * io.mem_rows * H;
+  const uint16_t* memv_l = io.memv + (size_t)l * io.mem_rows * H;
+  AttnParams ap;
+  memset(&ap, 0, sizeof(ap));
+  ap.y = h->y;
+  ap.T = q.T;
+  ap.qk_eps = h->d.qk_eps;
+  ap.scale = 1.0f / sqrtf((float)HD);
+  ap.lim_stride = io.lim_stride;
+  // self-attention block
+  seq_adarms(q, blk);
+  seq_gemm(q, G_QKV, l, 0, h->qkv, 3 * H, nullptr);
+  if (io.frame_row0 >= 0 && q.err == cudaSuccess && q.st == MKX_OK)
+    q.err = launch_pdl(bt_write_frame, dim3((q.M * NH + 7) / 8), dim3(256), 0, q.stream, (const uint16_t*)h->qkv, q.M,
+                       const_cast<uint16_t*>(memk_l), const_cast<uint16_t*>(memv_l), io.frame_row0,
+                       (const float*)(h->nrm + (size_t)(L + l) * HD), io.sa_cos, io.sa_sin, h->d.qk_eps);
+  ap.src = h->qkv;
+  ap.src_ld = 3 * H;
+  ap.kb = memk_l;
+  ap.vb = memv_l;
+  ap.kv_ep = io.kvm_ep;
+  ap.kv_rows = io.mem_rows;
+  ap.lim = io.kv_start;
+  ap.cos = io.sa_cos;
+  ap.sin = io.sa_sin;
+  ap.wq = h->nrm + (size_t)l * HD;
+  ap.wk = h->nrm + (size_t)(L + l) * HD;
+  ap.kcap = kcap;
+  ap.own = io.own;
+  if (q.err == cudaSuccess && q.st == MKX_OK)
+    q.err = launch_pdl(bt_attention<true>, dim3(q.B * NH), dim3(32 * ATT_WARPS), att_sa, q.stream, ap);
+  seq_gemm(q, G_O, l, 1, h->h, H, blk + 2 * H);
+  // cross-attention block
+  seq_adarms(q, blk + 3 * H);
+  seq_gemm(q, G_CAQ, l, 0, h->qkv, H, nullptr);  // the query in the qkv buffer, rows of H
+  ap.src = h->qkv;
+  ap.src_ld = H;
+  ap.kb = io.kca + (size_t)l * io.ca_rows * H;
+  ap.vb = io.vca + (size_t)l * io.ca_rows * H;
+  ap.kv_ep = io.kvc_ep;
+  ap.kv_rows = io.ca_rows;
+  ap.lim = io.src_rows;
+  ap.cos = io.ca_cos;
+  ap.sin = io.ca_sin;
+  ap.wq = h->nrm + (size_t)(2 * L + l) * HD;
+  ap.wk = nullptr;
+  if (q.err == cudaSuccess && q.st == MKX_OK)
+    q.err = launch_pdl(bt_attention<false>, dim3(q.B * NH), dim3(32 * ATT_WARPS), att_ca, q.stream, ap);
+  seq_gemm(q, G_OCA, l, 1, h->h, H, blk + 5 * H);
+  // MLP block
+  seq_adarms(q, blk + 6 * H);
+  seq_gemm(q, G_GU, l, 0, h->g, I, nullptr);
+  seq_gemm(q, G_D, l, 2, h->h, H, blk + 8 * H);
+}
+
+mkx_status seq_finish(Seq& q, const char* what) {
+  if (q.err != cudaSuccess) return batch_fail(q.err, what);
+  if (q.st != MKX_OK) {
+    snprintf(g_batch_err, sizeof(g_batch_err), "%s: tensor map or launch shape", what);
+    return q.st;
+  }
+  return MKX_OK;
+}
+}  // namespace
+
 extern "C" mkx_status mkx_batch_run(mkx_batch_handle* h, const mkx_batch_inputs* in, cudaStream_t stream) {
   if (!h || !in) return MKX_ERR_INVALID_ARG;
   const mkx_dims& d = h->d;
@@ -970,63 +1158,30 @@ extern "C" mkx_status mkx_batch_run(mkx_batch_handle* h, const mkx_batch_inputs*
     if (reinterpret_cast<uintptr_t>(q) & 7u) return MKX_ERR_INVALID_ARG;
   DeviceScope dev_scope(h->device);
   if (dev_scope.err != cudaSuccess) return batch_fail(dev_scope.err, "cudaSetDevice");
-  const int L = d.L, I = d.I, A = d.A, T = in->T, B = in->B;
-  const int M = B * T, Mp = ((M + 15) / 16) * 16;
+  const int L = d.L, A = d.A, T = in->T, B = in->B;
   const int MODW = 9 * L * H + 2 * H;
-  const long long ep_stride = (long long)(in->n_steps + 1) * MODW;
-  const long long kvm_ep = (long long)L * in->mem_rows * H, kvc_ep = (long long)L * in->ca_rows * H;
-  const float scale = 1.0f / sqrtf((float)HD);
-  const int kcap = (in->mem_rows + T + CA_BLK - 1) / CA_BLK * CA_BLK;  // <= SA_MAXK
-  const size_t att_sa = (size_t)(16 + 2 * kcap) * KS * 2;
-  const size_t att_ca = (size_t)(16 + 4 * CA_BLK) * KS * 2;
-  cudaError_t err = cudaSuccess;
-  mkx_status st = MKX_OK;
-  auto gemm = [&](int g, int l, int buf, uint16_t* out, int ldo, const uint16_t* gate) {
-    if (err != cudaSuccess || st != MKX_OK) return;
-    const GemmShape s = gemm_shape(g, I);
-    const int ntok = gemm_token_tile(M, s.ntiles, h->sms), ttiles = (M + ntok - 1) / ntok;
-    const CUtensorMap* map = token_map(h, buf, ntok);
-    GemmLaunch gl;
-    if (!map || !gemm_launch_shape(ntok, g != G_D && s.epi == E_GATED, &gl)) {
-      st = map ? MKX_ERR_UNSUPPORTED : MKX_ERR_CUDA;
-      return;
-    }
-    GemmParams p;
-    memset(&p, 0, sizeof(p));
-    p.wpk = h->wpk[g] + (size_t)l * s.ntiles * s.ktiles * (A_BYTES / 2);
-    p.ktiles = s.ktiles;
-    p.splits = g == G_D ? down_splits(s, ttiles, h->sms) : 1;
-    p.kps = (s.ktiles + p.splits - 1) / p.splits;
-    p.splits = (s.ktiles + p.kps - 1) / p.kps;
-    p.ntok = ntok;
-    p.M = M;
-    p.T = T;
-    p.epi = p.splits > 1 ? E_PARTIAL : s.epi;
-    if (p.epi != E_GATED && !gemm_launch_shape(ntok, false, &gl)) {
-      st = MKX_ERR_UNSUPPORTED;
-      return;
-    }
-    p.stages = gl.stages;
-    p.out = out;
-    p.ldo = ldo;
-    p.ws = h->ws;
-    p.Mp = Mp;
-    p.gate = gate;
-    p.gate_stride = ep_stride;
-    p.status = h->status;
-    p.timeout_ns = h->timeout_ns;
-    err = launch_pdl(bt_gemm, dim3(s.ntiles, ttiles, p.splits), dim3(GEMM_THREADS), (size_t)gl.smem, stream, *map, p);
-    if (err == cudaSuccess && p.splits > 1)
-      err = launch_pdl(bt_reduce_gated, dim3((M * (H / 2) + 255) / 256), dim3(256), 0, stream, (const float*)h->ws,
-                       p.splits, Mp, M, T, out, gate, ep_stride);
-  };
-  auto adarms = [&](const uint16_t* blk) {
-    if (err != cudaSuccess) return;
-    err = launch_pdl(bt_adarms, dim3((Mp + 7) / 8), dim3(256), 0, stream, (const uint16_t*)h->h, h->a, M, Mp, T, blk,
-                     ep_stride, d.eps);
-  };
+  Seq q = {h, stream, B, T, B * T, ((B * T + 15) / 16) * 16, (long long)(in->n_steps + 1) * MODW, cudaSuccess, MKX_OK};
+  LayerIO io;
+  memset(&io, 0, sizeof(io));
+  io.memk = in->memk;
+  io.memv = in->memv;
+  io.kvm_ep = (long long)L * in->mem_rows * H;
+  io.mem_rows = in->mem_rows;
+  io.kv_start = in->kv_start;
+  io.kca = in->kca;
+  io.vca = in->vca;
+  io.kvc_ep = (long long)L * in->ca_rows * H;
+  io.ca_rows = in->ca_rows;
+  io.src_rows = in->src_rows;
+  io.lim_stride = 1;
+  io.own = 1;
+  io.sa_cos = in->sa_cos;
+  io.sa_sin = in->sa_sin;
+  io.ca_cos = in->ca_cos;
+  io.ca_sin = in->ca_sin;
+  io.frame_row0 = -1;
   auto tail = [&](int first, int last, int s) {
-    if (err != cudaSuccess) return;
+    if (q.err != cudaSuccess) return;
     TailParams t;
     memset(&t, 0, sizeof(t));
     t.x_in = in->x_in;
@@ -1034,7 +1189,7 @@ extern "C" mkx_status mkx_batch_run(mkx_batch_handle* h, const mkx_batch_inputs*
     t.x_out = in->x_out;
     t.h = h->h;
     t.mfin = in->mods + (size_t)(1 + s) * MODW + (size_t)9 * L * H;
-    t.ep_stride = ep_stride;
+    t.ep_stride = q.ep_stride;
     t.dt = in->dt;
     t.win = h->win;
     t.bin = h->bin;
@@ -1046,68 +1201,61 @@ extern "C" mkx_status mkx_batch_run(mkx_batch_handle* h, const mkx_batch_inputs*
     t.first = first;
     t.last = last;
     t.eps = d.eps;
-    err = launch_pdl(bt_tail, dim3(M), dim3(256), 0, stream, t);
+    q.err = launch_pdl(bt_tail, dim3(q.M), dim3(256), 0, stream, t);
   };
   cudaMemsetAsync(h->status, 0, sizeof(int), stream);
   tail(1, 0, 0);  // h0 = in-projection of x_in
   for (int s = 0; s < in->n_steps; ++s) {
     const uint16_t* mrow = in->mods + (size_t)(1 + s) * MODW;
-    for (int l = 0; l < L; ++l) {
-      const uint16_t* blk = mrow + (size_t)9 * H * l;
-      AttnParams ap;
-      memset(&ap, 0, sizeof(ap));
-      ap.y = h->y;
-      ap.T = T;
-      ap.qk_eps = d.qk_eps;
-      ap.scale = scale;
-      // self-attention block
-      adarms(blk);
-      gemm(G_QKV, l, 0, h->qkv, 3 * H, nullptr);
-      ap.src = h->qkv;
-      ap.src_ld = 3 * H;
-      ap.kb = in->memk + (size_t)l * in->mem_rows * H;
-      ap.vb = in->memv + (size_t)l * in->mem_rows * H;
-      ap.kv_ep = kvm_ep;
-      ap.kv_rows = in->mem_rows;
-      ap.lim = in->kv_start;
-      ap.cos = in->sa_cos;
-      ap.sin = in->sa_sin;
-      ap.wq = h->nrm + (size_t)l * HD;
-      ap.wk = h->nrm + (size_t)(L + l) * HD;
-      ap.kcap = kcap;
-      if (err == cudaSuccess)
-        err = launch_pdl(bt_attention<true>, dim3(B * NH), dim3(32 * ATT_WARPS), att_sa, stream, ap);
-      gemm(G_O, l, 1, h->h, H, blk + 2 * H);
-      // cross-attention block
-      adarms(blk + 3 * H);
-      gemm(G_CAQ, l, 0, h->qkv, H, nullptr);  // the query in the qkv buffer, rows of H
-      ap.src = h->qkv;
-      ap.src_ld = H;
-      ap.kb = in->kca + (size_t)l * in->ca_rows * H;
-      ap.vb = in->vca + (size_t)l * in->ca_rows * H;
-      ap.kv_ep = kvc_ep;
-      ap.kv_rows = in->ca_rows;
-      ap.lim = in->src_rows;
-      ap.cos = in->ca_cos;
-      ap.sin = in->ca_sin;
-      ap.wq = h->nrm + (size_t)(2 * L + l) * HD;
-      ap.wk = nullptr;
-      if (err == cudaSuccess)
-        err = launch_pdl(bt_attention<false>, dim3(B * NH), dim3(32 * ATT_WARPS), att_ca, stream, ap);
-      gemm(G_OCA, l, 1, h->h, H, blk + 5 * H);
-      // MLP block
-      adarms(blk + 6 * H);
-      gemm(G_GU, l, 0, h->g, I, nullptr);
-      gemm(G_D, l, 2, h->h, H, blk + 8 * H);
-    }
+    for (int l = 0; l < L; ++l) seq_layer(q, l, mrow + (size_t)9 * H * l, io);
     tail(0, s + 1 == in->n_steps, s);
   }
-  if (err != cudaSuccess) return batch_fail(err, "mkx_batch_run launch");
-  if (st != MKX_OK) {
-    snprintf(g_batch_err, sizeof(g_batch_err), "mkx_batch_run: tensor map or launch shape");
-    return st;
-  }
-  return MKX_OK;
+  return seq_finish(q, "mkx_batch_run");
+}
+
+extern "C" mkx_status mkx_batch_register_pass(mkx_batch_handle* h, const mkx_register_inputs* in, cudaStream_t stream) {
+  if (!h || !in) return MKX_ERR_INVALID_ARG;
+  const mkx_dims& d = h->d;
+  if (in->R < 16 || in->R % 16 != 0 || in->R > 16 * h->max_ep || in->mem_rows < in->R || in->mem_rows > 256 ||
+      in->ca_rows < 1 || in->ca_rows > 4096)
+    return MKX_ERR_INVALID_ARG;
+  const void* ptrs[] = {in->reg_in, in->memk, in->memv, in->kv_start, in->kca, in->vca, in->src_rows,
+                        in->sa_cos, in->sa_sin, in->ca_cos, in->ca_sin};
+  for (const void* q : ptrs)
+    if (!q) return MKX_ERR_INVALID_ARG;
+  const void* al16[] = {in->reg_in, in->memk, in->memv, in->kca, in->vca};
+  for (const void* q : al16)
+    if (reinterpret_cast<uintptr_t>(q) & 15u) return MKX_ERR_INVALID_ARG;
+  const void* al8[] = {in->sa_cos, in->sa_sin, in->ca_cos, in->ca_sin};
+  for (const void* q : al8)
+    if (reinterpret_cast<uintptr_t>(q) & 7u) return MKX_ERR_INVALID_ARG;
+  DeviceScope dev_scope(h->device);
+  if (dev_scope.err != cudaSuccess) return batch_fail(dev_scope.err, "cudaSetDevice");
+  const int L = d.L, R = in->R;
+  // the register rows as R / 16 groups of 16 query rows sharing one memory and one source; plain
+  // norms and residuals: one modulation row of zero scale / shift and unit gates for every group
+  Seq q = {h, stream, R / 16, 16, R, R, 0, cudaSuccess, MKX_OK};
+  LayerIO io;
+  memset(&io, 0, sizeof(io));
+  io.memk = in->memk;
+  io.memv = in->memv;
+  io.mem_rows = in->mem_rows;
+  io.kv_start = in->kv_start;
+  io.kca = in->kca;
+  io.vca = in->vca;
+  io.ca_rows = in->ca_rows;
+  io.src_rows = in->src_rows;
+  io.lim_stride = 0;
+  io.own = 0;
+  io.sa_cos = in->sa_cos;
+  io.sa_sin = in->sa_sin;
+  io.ca_cos = in->ca_cos;
+  io.ca_sin = in->ca_sin;
+  io.frame_row0 = in->mem_rows - R;
+  cudaMemsetAsync(h->status, 0, sizeof(int), stream);
+  q.err = cudaMemcpyAsync(h->h, in->reg_in, (size_t)R * H * 2, cudaMemcpyDeviceToDevice, stream);
+  for (int l = 0; l < L; ++l) seq_layer(q, l, h->plain + (size_t)9 * H * l, io);
+  return seq_finish(q, "mkx_batch_register_pass");
 }
 
 extern "C" const char* mkx_batch_last_cuda_error(void) { return g_batch_err; }
@@ -1141,7 +1289,7 @@ extern "C" void mkx_batch_destroy(mkx_batch_handle* h) {
   if (!h) return;
   DeviceScope dev_scope(h->device);
   for (int g = 0; g < NGEMM; ++g) cudaFree(h->wpk[g]);
-  void* bufs[] = {h->nrm, h->win, h->bin, h->wout, h->bout, h->h, h->a, h->qkv, h->y, h->g,
+  void* bufs[] = {h->nrm, h->plain, h->win, h->bin, h->wout, h->bout, h->h, h->a, h->qkv, h->y, h->g,
                   h->xs, h->ws, h->status};
   for (void* b : bufs) cudaFree(b);
   delete h;

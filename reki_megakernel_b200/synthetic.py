@@ -261,6 +261,23 @@ def make_source(S: int, src_dim: int = 2048, seed: int = 0) -> torch.Tensor:
     return (torch.randn((S, src_dim), generator=g) * 0.5).to(torch.bfloat16)
 
 
+def make_register_rows(dims: ExpertDims, R: int = 32, seed: int = 0) -> torch.Tensor:
+    """The register rows entering layer 0 of the register pass, [R, H] bf16: a seeded N(0, 0.02)
+    learned embedding, the same for every frame (restated: Kyutai's register tokens are not in the
+    reference checkout; what differs between frames is the source and the carried memory)."""
+    g = torch.Generator().manual_seed(seed + 37)
+    return (torch.randn((R, dims.H), generator=g) * 0.02).to(torch.bfloat16)
+
+
+def register_rope(dims: ExpertDims, PM: int, R: int):
+    """RoPE tables (fp32 [R, HD]) of the register rows: (sa_cos, sa_sin) at self-attention positions
+    PM - R .. PM - 1 -- the memory rows the frame is written to; a frame is not re-rotated when later
+    frames push it up -- and (ca_cos, ca_sin) at cross-attention positions 0 .. R - 1."""
+    sa = rope_cos_sin(torch.arange(R) + (PM - R), dims.HD)
+    ca = rope_cos_sin(torch.arange(R), dims.HD)
+    return sa[0], sa[1], ca[0], ca[1]
+
+
 @dataclass
 class ModulationWeights:
     """Weights of the restated per-step modulation network (the GPU ``StepModulations``): timestep

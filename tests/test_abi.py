@@ -58,7 +58,8 @@ def _c_layout(struct: str, fields):
 
 @pytest.mark.parametrize("struct,cls", [("mkx_dims", "Dims"), ("mkx_weights", "Weights"), ("mkx_step_inputs", "StepInputs"),
                                         ("mkx_packed_weights", "PackedWeights"), ("mkx_prep_dims", "PrepDims"),
-                                        ("mkx_batch_inputs", "BatchInputs")])
+                                        ("mkx_batch_inputs", "BatchInputs"),
+                                        ("mkx_register_inputs", "RegisterInputs")])
 def test_struct_layout_matches_c(struct, cls):
     from reki_megakernel_b200 import _lib
     ct = getattr(_lib, cls)
@@ -114,6 +115,7 @@ def test_batch_arguments_are_rejected_without_a_device():
     assert lib.mkx_batch_launches(None, 8, 10, 9) == -1
     assert lib.mkx_batch_last_error(None, None) == _lib.MKX_ERR_INVALID_ARG
     assert lib.mkx_batch_copy_state(None, 0, None, 0) == _lib.MKX_ERR_INVALID_ARG
+    assert lib.mkx_batch_register_pass(None, None, None) == _lib.MKX_ERR_INVALID_ARG
     lib.mkx_batch_destroy(None)
 
 
