@@ -58,7 +58,7 @@ typedef struct {
 mkx_status mkx_batch_create(const mkx_dims* dims, const mkx_weights* w, int max_episodes, int device,
                             mkx_batch_handle** out);
 
-/* Enqueues the whole loop (11 or 12 launches per layer and Euler step, see mkx_batch_launches) on
+/* Enqueues the whole loop (11 launches per layer and Euler step, see mkx_batch_launches) on
  * `stream`, each launch a programmatic dependent of the one before; no host
  * synchronisation, capturable in a CUDA graph. One run in flight per handle. */
 mkx_status mkx_batch_run(mkx_batch_handle* h, const mkx_batch_inputs* in, cudaStream_t stream);
@@ -89,7 +89,7 @@ typedef struct {
   int R;                    /* register rows: a multiple of 16, <= 16 * max_episodes */
 } mkx_register_inputs;
 
-/* Enqueues the register pass on `stream` (12 or 13 launches per layer, programmatic dependents, no
+/* Enqueues the register pass on `stream` (12 launches per layer, programmatic dependents, no
  * host synchronisation, capturable). Uses the handle's activation buffers: not concurrent with
  * mkx_batch_run on the same handle. */
 mkx_status mkx_batch_register_pass(mkx_batch_handle* h, const mkx_register_inputs* in, cudaStream_t stream);

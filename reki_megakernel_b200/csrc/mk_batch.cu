@@ -12,9 +12,12 @@
 // 128-byte-swizzled, tile-contiguous 16 KB blocks: one bulk copy each) and the token rows (TMA with
 // the same swizzle) into an mbarrier ring; warp 1 issues tcgen05.mma kind::f16 (M 128, N ntok, K 16)
 // into a TMEM accumulator; warps 2-5 read it back (tcgen05.ld) into a transposed fp32 tile in the
-// drained ring; then all six warps run the epilogue with 4-byte coalesced stores. The down projection
-// (K = 3072, 6 feature tiles) splits K over several CTAs that write fp32 partials; a reduction kernel
-// over all token rows adds them in split order and applies the gated residual. The W stream
+// drained ring; then all six warps run the epilogue with 4-byte coalesced stores. A GEMM with too few
+// tiles to cover the SMs splits K over a thread-block cluster of up to 8 CTAs: each keeps its fp32
+// partial tile in shared memory, and after a cluster barrier every CTA adds one slice of token rows
+// over the cluster (distributed shared memory, split order) and runs the epilogue on it. Up to 128
+// token rows the split depends only on the GEMM's shape, so a row's result does not depend on the
+// other rows of the launch. The W stream
 // does not depend on the previous kernel, so each GEMM is launched as a programmatic dependent: its
 // producer starts the W copies before griddepcontrol.wait and only the token-row loads wait for the
 // previous kernel. Every wait on an mbarrier is bounded by %globaltimer; after a timeout the CTA
@@ -36,25 +39,46 @@ namespace mkxb {
 using namespace mkx;
 
 constexpr int H = 768, NH = 12, HD = 64, AO = 8, TPMAX = 16;
-constexpr int BM = 128, BK = 64, MAXN = 256, MAX_STAGES = 8, GEMM_THREADS = 192, TMEM_COLS = 256;
+constexpr int BM = 128, BK = 64, MAXN = 256, MAX_STAGES = 8, GEMM_THREADS = 192;
 constexpr int A_BYTES = BM * BK * 2;
 constexpr int SMEM_BUDGET = 227 * 1024;
 constexpr int TS = BM + 4;  // transposed accumulator tile: floats per token row
-constexpr int MAX_SPLITS = 32;
-enum Epi { E_STORE = 0, E_GATED = 1, E_GU = 2, E_PARTIAL = 3 };
+constexpr int MAX_SPLITS = 8;  // K splits of one GEMM tile: the last CTA of a tile reads them all back
+constexpr int SMALL_M = 128;   // token rows up to which a GEMM is one token tile with a shape-fixed K split
+enum Epi { E_STORE = 0, E_GATED = 1, E_GU = 2 };
 enum Gemm { G_QKV = 0, G_O, G_CAQ, G_OCA, G_GU, G_D, NGEMM };
 
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
+// thread-block clusters: rank, barrier (release / acquire: shared-memory writes before it are visible
+// to the cluster after it), and loads from another CTA's shared memory
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t map_cluster(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr)
+               : "memory");
+  return v;
+}
+
 struct GemmParams {
   const uint16_t* wpk;      // this layer's W tiles: [ntiles][ktiles] blocks of A_BYTES
   int ktiles, kps, splits;  // k tiles in all, per split, splits
-  int ntok, M, T, stages, epi;
+  int ntok, M, T, stages, epi, ttiles, tmem_cols;
   uint16_t* out;            // bf16 [M][ldo]
   int ldo;
-  float* ws;                // E_PARTIAL: fp32 partials [split][Mp][ldo]
-  int Mp;
   const uint16_t* gate;     // E_GATED: gate of episode e, feature f at gate[e * gate_stride + f]
   long long gate_stride;
   int* status;
@@ -103,11 +127,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) bt_gemm(const __grid_constant
     *consumed_slot = 0;
     fence_mbar_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+  if (warp == 1) tmem_alloc(tmem_slot, (uint32_t)p.tmem_cols);
   __syncthreads();
   tmem_fence_after();
   const uint32_t tmem = *tmem_slot;
   int issued = 0;
+  if (threadIdx.x == 0) grid_dep_launch();  // the next kernel's CTAs may take free SMs and start their W
 
   if (warp == 0 && lane == 0) {
     // producer: the W tiles of the first stages need nothing from the previous kernel
@@ -182,14 +207,40 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) bt_gemm(const __grid_constant
     tmem_fence_before();
   }
   ok = __syncthreads_and(ok);
-  if (threadIdx.x == 0) grid_dep_launch();  // the next kernel may start its own weight stream
   const int nv = min(p.ntok, p.M - tok0);   // valid token rows of this tile
+  // split K: the splits of one tile form a thread-block cluster; each holds its fp32 partial tile in
+  // its own shared memory. After a cluster barrier CTA r sums rows [r0, r1) of every partial, in split
+  // order (the same order in every CTA: deterministic), into its own tile -- no other CTA reads those
+  // rows from it -- and runs the epilogue on them; a second barrier before exit keeps every tile
+  // readable until the whole cluster is done with it.
+  int r0 = 0, r1 = nv;
+  if (p.splits > 1) {
+    const int per = (nv + p.splits - 1) / p.splits;
+    r0 = min(nv, (int)cluster_ctarank() * per);
+    r1 = min(nv, r0 + per);
+    cluster_sync();
+    const uint32_t base = smem_u32(tsm);
+    for (int i = threadIdx.x; i < (r1 - r0) * (BM / 4); i += GEMM_THREADS) {
+      const int tl = r0 + i / (BM / 4), c = i % (BM / 4);
+      const uint32_t off = (uint32_t)(tl * TS + 4 * c) * 4u;
+      float4 acc = ld_cluster_f4(map_cluster(base + off, 0));
+      for (int z = 1; z < p.splits; ++z) {
+        const float4 t = ld_cluster_f4(map_cluster(base + off, (uint32_t)z));
+        acc.x += t.x;
+        acc.y += t.y;
+        acc.z += t.z;
+        acc.w += t.w;
+      }
+      *reinterpret_cast<float4*>(tsm + tl * TS + 4 * c) = acc;
+    }
+    __syncthreads();
+  }
   if (ok) {
     if (p.epi == E_GU) {
       // rows 0..63 of the tile are gate rows, 64..127 the up rows of the same 64 columns:
       // g = bf16(silu(bf16(gate)) * bf16(up)) (src/mk_expert.py:403-413)
-      for (int i = threadIdx.x; i < nv * 32; i += GEMM_THREADS) {
-        const int tl = i >> 5, cp = i & 31;
+      for (int i = threadIdx.x; i < (r1 - r0) * 32; i += GEMM_THREADS) {
+        const int tl = r0 + (i >> 5), cp = i & 31;
         const float2 gt = *reinterpret_cast<const float2*>(tsm + tl * TS + 2 * cp);
         const float2 up = *reinterpret_cast<const float2*>(tsm + tl * TS + 64 + 2 * cp);
         const float g0 = round_bf(gt.x), g1 = round_bf(gt.y);
@@ -201,7 +252,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) bt_gemm(const __grid_constant
       // items (token tl, feature pair fp), 8 per thread per round: every load of a round is issued
       // before its stores, so the round costs one memory latency, not eight
       constexpr int U = 8;
-      const int n = nv * (BM / 2);
+      const int n = (r1 - r0) * (BM / 2);
       for (int base = threadIdx.x; base < n; base += GEMM_THREADS * U) {
         float2 v[U];
         uint32_t rv[U], gv[U];
@@ -211,7 +262,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) bt_gemm(const __grid_constant
           rv[k] = gv[k] = 0u;
           v[k] = make_float2(0.f, 0.f);
           if (i < n) {
-            const int tl = i / (BM / 2), fp = i % (BM / 2);
+            const int tl = r0 + i / (BM / 2), fp = i % (BM / 2);
             const int m = tok0 + tl, f = tile * BM + 2 * fp;
             v[k] = *reinterpret_cast<const float2*>(tsm + tl * TS + 2 * fp);
             if (p.epi == E_GATED) {
@@ -224,22 +275,19 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) bt_gemm(const __grid_constant
         for (int k = 0; k < U; ++k) {
           const int i = base + GEMM_THREADS * k;
           if (i >= n) break;
-          const int tl = i / (BM / 2), fp = i % (BM / 2);
+          const int tl = r0 + i / (BM / 2), fp = i % (BM / 2);
           const int m = tok0 + tl, f = tile * BM + 2 * fp;
-          if (p.epi == E_PARTIAL) {
-            *reinterpret_cast<float2*>(p.ws + ((size_t)split * p.Mp + m) * p.ldo + f) = v[k];
-          } else {
-            uint32_t* dst = reinterpret_cast<uint32_t*>(p.out + (size_t)m * p.ldo + f);
-            if (p.epi == E_STORE)
-              *dst = pack_bf2(v[k].x, v[k].y);
-            else  // gated residual bf16(res + bf16(acc) * gate) (src/mk_expert.py:162-172), in place
-              *dst = pack_bf2(fmaf(round_bf(v[k].x), bf_lo(gv[k]), bf_lo(rv[k])),
-                              fmaf(round_bf(v[k].y), bf_hi(gv[k]), bf_hi(rv[k])));
-          }
+          uint32_t* dst = reinterpret_cast<uint32_t*>(p.out + (size_t)m * p.ldo + f);
+          if (p.epi == E_STORE)
+            *dst = pack_bf2(v[k].x, v[k].y);
+          else  // gated residual bf16(res + bf16(acc) * gate) (src/mk_expert.py:162-172), in place
+            *dst = pack_bf2(fmaf(round_bf(v[k].x), bf_lo(gv[k]), bf_lo(rv[k])),
+                            fmaf(round_bf(v[k].y), bf_hi(gv[k]), bf_hi(rv[k])));
         }
       }
     }
   }
+  if (p.splits > 1) cluster_sync();  // no CTA leaves while another may still read its partial tile
   __syncthreads();
   if (threadIdx.x == 0) {
     for (int i = *consumed_slot; i < issued; ++i)
@@ -248,30 +296,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) bt_gemm(const __grid_constant
   if (warp == 1) {
     wait_bounded(done, 0, p.timeout_ns);
     tmem_fence_after();
-    tmem_free(tmem, TMEM_COLS);
+    tmem_free(tmem, (uint32_t)p.tmem_cols);
   }
-}
-
-// Split-K reduction of the down projection: h[m][f] = bf16(h + bf16(sum_z ws[z][m][f]) * gate_e[f]),
-// the splits added in order; one thread per column pair.
-__global__ void __launch_bounds__(256) bt_reduce_gated(const float* __restrict__ ws, int splits, int Mp, int M, int T,
-                                                       uint16_t* h, const uint16_t* __restrict__ gate,
-                                                       long long gate_stride) {
-  grid_dep_wait();
-  if (threadIdx.x == 0) grid_dep_launch();
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= M * (H / 2)) return;
-  const int m = i / (H / 2), f = 2 * (i % (H / 2));
-  float2 acc = *reinterpret_cast<const float2*>(ws + (size_t)m * H + f);
-  for (int z = 1; z < splits; ++z) {
-    const float2 t = *reinterpret_cast<const float2*>(ws + ((size_t)z * Mp + m) * H + f);
-    acc.x += t.x;
-    acc.y += t.y;
-  }
-  uint32_t* dst = reinterpret_cast<uint32_t*>(h + (size_t)m * H + f);
-  const uint32_t rv = *dst;
-  const uint32_t gv = *reinterpret_cast<const uint32_t*>(gate + (size_t)(m / T) * gate_stride + f);
-  *dst = pack_bf2(fmaf(round_bf(acc.x), bf_lo(gv), bf_lo(rv)), fmaf(round_bf(acc.y), bf_hi(gv), bf_hi(rv)));
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -795,8 +821,6 @@ struct mkx_batch_handle {
   float *win, *bin, *wout, *bout;
   uint16_t *h, *a, *qkv, *y, *g;
   float* xs;
-  float* ws;
-  size_t ws_floats;
   int* status;
   unsigned long long timeout_ns;
   // tensor maps of the GEMM B operands (AdaRMS rows, attention output, gate/up product) per token
@@ -835,7 +859,6 @@ extern "C" mkx_status mkx_batch_create(const mkx_dims* dims, const mkx_weights* 
   const int L = d.L, I = d.I, A = d.A;
   const int Mp = ((max_episodes * TPMAX + 15) / 16) * 16;
   h->Mp_max = Mp;
-  h->ws_floats = (size_t)MAX_SPLITS * Mp * H;  // split-K partials of the down projection
   bool ok = true;
   auto alloc = [&](void** pp, size_t bytes) {
     if (ok && cudaMalloc(pp, bytes) != cudaSuccess) ok = false;
@@ -856,7 +879,6 @@ extern "C" mkx_status mkx_batch_create(const mkx_dims* dims, const mkx_weights* 
   alloc((void**)&h->y, (size_t)Mp * H * 2);
   alloc((void**)&h->g, (size_t)Mp * I * 2);
   alloc((void**)&h->xs, (size_t)max_episodes * TPMAX * A * 4);
-  alloc((void**)&h->ws, h->ws_floats * 4);
   alloc((void**)&h->status, 64);
   if (!ok) {
     mkx_batch_destroy(h);
@@ -915,19 +937,34 @@ extern "C" mkx_status mkx_batch_create(const mkx_dims* dims, const mkx_weights* 
 
 namespace {
 // Launch with the programmatic-dependent attribute (the kernel waits for its predecessor itself).
+// cluster_z > 1: thread-block clusters of (1, 1, cluster_z) CTAs.
 template <typename... KArgs, typename... Args>
-cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+cudaError_t launch_pdl_cluster(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, int cluster_z,
+                               Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute at[1];
+  cudaLaunchAttribute at[2];
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   at[0].val.programmaticStreamSerializationAllowed = 1;
+  int n = 1;
+  if (cluster_z > 1) {
+    at[1].id = cudaLaunchAttributeClusterDimension;
+    at[1].val.clusterDim.x = 1;
+    at[1].val.clusterDim.y = 1;
+    at[1].val.clusterDim.z = (unsigned)cluster_z;
+    n = 2;
+  }
   cfg.attrs = at;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = n;
   return cudaLaunchKernelEx(&cfg, k, args...);
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+  return launch_pdl_cluster(k, grid, block, smem, st, 1, args...);
 }
 
 // Token tile of a GEMM with `ntiles` feature tiles: about one CTA per SM (each token tile re-reads the
@@ -943,37 +980,50 @@ int gemm_token_tile(int M, int ntiles, int sms) {
 }
 
 struct GemmLaunch {
-  int stages, smem;
+  int stages, smem, tmem_cols;
 };
-// Ring stages for a token tile: as many as fit next to the barriers (and, gated epilogues, the
-// residual tile); the transposed accumulator tile reuses the ring. >= 80 KB: at most 2 CTAs
-// (2 x 256 TMEM columns) per SM, so no TMEM allocation waits. false if the accumulator tile does not fit.
-bool gemm_launch_shape(int ntok, bool residual, GemmLaunch* out) {
+// Ring stages for a token tile of a CTA with nk k tiles: no more than its k tiles (a short K range
+// leaves room for more CTAs per SM, so the next kernel's CTAs can start their weight streams while
+// this one finishes) and no more than fit next to the barriers (and, gated epilogues, the residual
+// tile); the transposed accumulator tile reuses the ring. TMEM: ntok columns rounded up to a power
+// of two >= 32; the shared-memory size is raised so that no more CTAs fit on an SM than their TMEM
+// columns allow (512 per SM), so a TMEM allocation never waits. false if the accumulator tile does not
+// fit.
+bool gemm_launch_shape(int ntok, bool residual, int nk, GemmLaunch* out) {
   const int stage_bytes = A_BYTES + ntok * BK * 2, slack = 1024 + 256, extra = residual ? ntok * BM * 2 : 0;
-  int st = (SMEM_BUDGET - slack - extra) / stage_bytes;
-  if (st > MAX_STAGES) st = MAX_STAGES;
-  if (st < 2 || ((ntok + 31) / 32) * 32 * TS * 4 > st * stage_bytes) return false;
+  int fit = (SMEM_BUDGET - slack - extra) / stage_bytes;
+  if (fit > MAX_STAGES) fit = MAX_STAGES;
+  const int tile_bytes = ((ntok + 31) / 32) * 32 * TS * 4;
+  int st = nk < fit ? nk : fit;
+  if (st < 1) st = 1;
+  while (st < fit && st * stage_bytes < tile_bytes) ++st;
+  if (st * stage_bytes < tile_bytes) return false;
+  int cols = 32;
+  while (cols < ntok) cols *= 2;
   out->stages = st;
+  out->tmem_cols = cols;
   out->smem = st * stage_bytes + slack + extra;
-  if (out->smem < 80 * 1024) out->smem = 80 * 1024;
-  return true;
+  const int per_sm = 512 / cols, floor_bytes = 228 * 1024 / (per_sm + 1) + 1024;
+  if (out->smem < floor_bytes) out->smem = floor_bytes;
+  return out->smem <= SMEM_BUDGET;
 }
 
-// K splits of the down projection: enough CTAs to cover the SMs, >= 4 k tiles (256 K) each.
-int down_splits(const GemmShape& s, int ttiles, int sms) {
-  const int ctas = s.ntiles * ttiles;
-  int z = (sms + ctas - 1) / ctas;
-  if (z > s.ktiles / 4) z = s.ktiles / 4;
+// K splits of a GEMM (one thread-block cluster per tile): as many as keep the launch within one wave
+// of CTAs (floor of SMs / tiles), at least 2 k tiles (128 K) each, at most MAX_SPLITS (the portable
+// cluster size).
+int gemm_splits(const GemmShape& s, int ttiles, int sms) {
+  int z = sms / (s.ntiles * ttiles);
+  if (z > s.ktiles / 2) z = s.ktiles / 2;
   if (z > MAX_SPLITS) z = MAX_SPLITS;
-  return z < 1 ? 1 : z;
+  if (z < 1) z = 1;
+  const int kps = (s.ktiles + z - 1) / z;
+  return (s.ktiles + kps - 1) / kps;
 }
 }  // namespace
 
 extern "C" int mkx_batch_launches(const mkx_batch_handle* h, int B, int T, int n_steps) {
   if (!h || B < 1 || B > h->max_ep || T < 1 || T > TPMAX || n_steps < 1) return -1;
-  const int M = B * T, ntok = gemm_token_tile(M, H / BM, h->sms), ttiles = (M + ntok - 1) / ntok;
-  const int reduce = down_splits(gemm_shape(G_D, h->d.I), ttiles, h->sms) > 1 ? 1 : 0;
-  return 1 + n_steps * ((11 + reduce) * h->d.L + 1);
+  return 1 + n_steps * (11 * h->d.L + 1);
 }
 
 namespace {
@@ -1006,16 +1056,21 @@ void seq_gemm(Seq& q, int g, int l, int buf, uint16_t* out, int ldo, const uint1
   if (q.err != cudaSuccess || q.st != MKX_OK) return;
   mkx_batch_handle* h = q.h;
   const GemmShape s = gemm_shape(g, h->d.I);
-  const int ntok = gemm_token_tile(q.M, s.ntiles, h->sms), ttiles = (q.M + ntok - 1) / ntok;
+  // up to SMALL_M token rows: one token tile and a K split fixed by the GEMM's shape, so a row's
+  // result does not depend on how many other rows share the launch; beyond, token tiles for about
+  // one CTA per SM and K splits only while the launch stays within one wave
+  const bool small = q.M <= SMALL_M;
+  const int ntok = small ? (q.M + 15) / 16 * 16 : gemm_token_tile(q.M, s.ntiles, h->sms);
+  const int ttiles = (q.M + ntok - 1) / ntok;
   const CUtensorMap* map = token_map(h, buf, ntok);
   GemmParams p;
   memset(&p, 0, sizeof(p));
-  p.splits = g == G_D ? down_splits(s, ttiles, h->sms) : 1;
+  p.splits = gemm_splits(s, ttiles, h->sms);
   p.kps = (s.ktiles + p.splits - 1) / p.splits;
-  p.splits = (s.ktiles + p.kps - 1) / p.kps;
-  p.epi = p.splits > 1 ? E_PARTIAL : s.epi;
+  p.epi = s.epi;
+  p.ttiles = ttiles;
   GemmLaunch gl;
-  if (!map || !gemm_launch_shape(ntok, p.epi == E_GATED, &gl)) {
+  if (!map || !gemm_launch_shape(ntok, p.epi == E_GATED, p.kps, &gl)) {
     q.st = map ? MKX_ERR_UNSUPPORTED : MKX_ERR_CUDA;
     return;
   }
@@ -1025,18 +1080,15 @@ void seq_gemm(Seq& q, int g, int l, int buf, uint16_t* out, int ldo, const uint1
   p.M = q.M;
   p.T = q.T;
   p.stages = gl.stages;
+  p.tmem_cols = gl.tmem_cols;
   p.out = out;
   p.ldo = ldo;
-  p.ws = h->ws;
-  p.Mp = q.Mp;
   p.gate = gate;
   p.gate_stride = q.ep_stride;
   p.status = h->status;
   p.timeout_ns = h->timeout_ns;
-  q.err = launch_pdl(bt_gemm, dim3(s.ntiles, ttiles, p.splits), dim3(GEMM_THREADS), (size_t)gl.smem, q.stream, *map, p);
-  if (q.err == cudaSuccess && p.splits > 1)
-    q.err = launch_pdl(bt_reduce_gated, dim3((q.M * (H / 2) + 255) / 256), dim3(256), 0, q.stream, (const float*)h->ws,
-                       p.splits, q.Mp, q.M, q.T, out, gate, q.ep_stride);
+  q.err = launch_pdl_cluster(bt_gemm, dim3(s.ntiles, ttiles, p.splits), dim3(GEMM_THREADS), (size_t)gl.smem, q.stream,
+                             p.splits, *map, p);
 }
 
 void seq_adarms(Seq& q, const uint16_t* blk) {
@@ -1290,7 +1342,7 @@ extern "C" void mkx_batch_destroy(mkx_batch_handle* h) {
   DeviceScope dev_scope(h->device);
   for (int g = 0; g < NGEMM; ++g) cudaFree(h->wpk[g]);
   void* bufs[] = {h->nrm, h->plain, h->win, h->bin, h->wout, h->bout, h->h, h->a, h->qkv, h->y, h->g,
-                  h->xs, h->ws, h->status};
+                  h->xs, h->status};
   for (void* b : bufs) cudaFree(b);
   delete h;
 }
