@@ -380,38 +380,33 @@ __device__ __forceinline__ void ldsm_x4_t(const void* p, uint32_t& r0, uint32_t&
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                : "r"(smem_u32(p)));
 }
-// Scores of the 16 query rows against 64 keys starting at shared row `k0` of Ks (c[nt]: keys
-// 8 nt + 2 cc, +1 of rows g and g + 8, unscaled). The B operand K^T comes from K rows by ldmatrix.
-__device__ __forceinline__ void scores64(const uint32_t (&qa)[4][4], const uint16_t* Ks, int k0, int lane,
-                                         float (&c)[8][4]) {
+// Scores of the 16 query rows against the 16 keys at shared rows [k0, k0 + 16) of Ks: two n8 tiles (c[nt]:
+// keys 8 nt + 2 cc, +1 of rows g and g + 8, unscaled). The B operand K^T comes from K rows by ldmatrix.
+__device__ __forceinline__ void scores16(const uint32_t (&qa)[4][4], const uint16_t* Ks, int k0, int lane,
+                                         float (&c)[2][4]) {
   const int mat = lane >> 3, r = lane & 7;
 #pragma unroll
-  for (int nt = 0; nt < 8; ++nt) c[nt][0] = c[nt][1] = c[nt][2] = c[nt][3] = 0.f;
+  for (int nt = 0; nt < 2; ++nt) c[nt][0] = c[nt][1] = c[nt][2] = c[nt][3] = 0.f;
 #pragma unroll
-  for (int ks = 0; ks < 4; ++ks)
-#pragma unroll
-    for (int np = 0; np < 4; ++np) {
-      uint32_t b0, b1, b2, b3;  // n-tile 2 np: (b0, b1); n-tile 2 np + 1: (b2, b3)
-      ldsm_x4(Ks + (size_t)(k0 + 16 * np + 8 * (mat >> 1) + r) * KS + 16 * ks + 8 * (mat & 1), b0, b1, b2, b3);
-      mma_bf16(c[2 * np], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b0, b1);
-      mma_bf16(c[2 * np + 1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b2, b3);
-    }
+  for (int ks = 0; ks < 4; ++ks) {
+    uint32_t b0, b1, b2, b3;
+    ldsm_x4(Ks + (size_t)(k0 + 8 * (mat >> 1) + r) * KS + 16 * ks + 8 * (mat & 1), b0, b1, b2, b3);
+    mma_bf16(c[0], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b0, b1);
+    mma_bf16(c[1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b2, b3);
+  }
 }
 
-// o += P (bf16, from the score fragments) . V[64 keys from shared row k0], V read transposed by ldmatrix.
-__device__ __forceinline__ void pv64(const float (&pc)[8][4], const uint16_t* Vs, int k0, int lane, float (&o)[8][4]) {
+// o += P V over the 16 keys [k0, k0 + 16): P (bf16 values in fp32) as the A operand, V by ldmatrix.trans.
+__device__ __forceinline__ void pv16(const float (&pc)[2][4], const uint16_t* Vs, int k0, int lane, float (&o)[8][4]) {
   const int mat = lane >> 3, r = lane & 7;
+  const uint32_t a0 = pack_bf2(pc[0][0], pc[0][1]), a1 = pack_bf2(pc[0][2], pc[0][3]);
+  const uint32_t a2 = pack_bf2(pc[1][0], pc[1][1]), a3 = pack_bf2(pc[1][2], pc[1][3]);
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const uint32_t a0 = pack_bf2(pc[2 * j][0], pc[2 * j][1]), a1 = pack_bf2(pc[2 * j][2], pc[2 * j][3]);
-    const uint32_t a2 = pack_bf2(pc[2 * j + 1][0], pc[2 * j + 1][1]), a3 = pack_bf2(pc[2 * j + 1][2], pc[2 * j + 1][3]);
-#pragma unroll
-    for (int dp = 0; dp < 4; ++dp) {
-      uint32_t b0, b1, b2, b3;
-      ldsm_x4_t(Vs + (size_t)(k0 + 16 * j + 8 * (mat & 1) + r) * KS + 16 * dp + 8 * (mat >> 1), b0, b1, b2, b3);
-      mma_bf16(o[2 * dp], a0, a1, a2, a3, b0, b1);
-      mma_bf16(o[2 * dp + 1], a0, a1, a2, a3, b2, b3);
-    }
+  for (int dp = 0; dp < 4; ++dp) {
+    uint32_t b0, b1, b2, b3;
+    ldsm_x4_t(Vs + (size_t)(k0 + 8 * (mat & 1) + r) * KS + 16 * dp + 8 * (mat >> 1), b0, b1, b2, b3);
+    mma_bf16(o[2 * dp], a0, a1, a2, a3, b0, b1);
+    mma_bf16(o[2 * dp + 1], a0, a1, a2, a3, b2, b3);
   }
 }
 
@@ -443,6 +438,7 @@ struct AttnParams {
 };
 
 constexpr int ATT_WARPS = 4;
+constexpr int OPS = HD + 4;  // floats per row of a warp's partial attention output
 
 template <bool SA>
 __global__ void __launch_bounds__(32 * ATT_WARPS) bt_attention(const __grid_constant__ AttnParams p) {
@@ -450,6 +446,7 @@ __global__ void __launch_bounds__(32 * ATT_WARPS) bt_attention(const __grid_cons
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, cc = lane & 3, T = p.T;
   if (tid == 0) grid_dep_launch();
   extern __shared__ __align__(16) char asmem[];
+  __shared__ float st_s[ATT_WARPS][16][2];  // per warp and query row: softmax max, sum
   const int e = blockIdx.x / NH, h = blockIdx.x % NH;
   uint16_t* Qs = reinterpret_cast<uint16_t*>(asmem);             // [16][KS]
   uint16_t* Ks = Qs + 16 * KS;                                    // SA: [SA_MAXK][KS]; CA: [2][64][KS]
@@ -458,7 +455,6 @@ __global__ void __launch_bounds__(32 * ATT_WARPS) bt_attention(const __grid_cons
   const uint16_t* vb = p.vb + (size_t)e * p.kv_ep + h * HD;
   const uint32_t zero = 0u;
   // key rows [k0, k0 + nrows) of K and V into shared rows [dst, dst + nrows) (asynchronous copies)
-  // (the first block's copies and the query rows use all warps; the math and later blocks, warp 0)
   auto stage = [&](int k0, int nrows, int dst, int t0, int nt) {
     for (int c = t0; c < nrows * 8; c += nt) {
       const int j = c >> 3, q = c & 7;
@@ -510,99 +506,111 @@ __global__ void __launch_bounds__(32 * ATT_WARPS) bt_attention(const __grid_cons
     }
     reinterpret_cast<uint32_t*>(Qs + (size_t)t * KS)[lane] = qv;
   }
-  cp_async_wait<0>();  // this thread's share of the first copies
-  __syncthreads();
-  if (warp != 0) return;
+  // Every warp takes the 16-key slice [64 b + 16 warp, + 16) of each 64-key block b, with its own
+  // softmax statistics (rows g and g + 8 of the quad's lanes); the warps' partial results are merged
+  // at the end. SA: the max over all keys first, then P = bf16(exp(s - max)) against it (the
+  // reference's two passes); CA: an online softmax over the warp's slices, the blocks double-buffered
+  // in shared memory with the next block's copy in flight.
   uint32_t qa[4][4];
-  {
+  float o[8][4];
+#pragma unroll
+  for (int dn = 0; dn < 8; ++dn) o[dn][0] = o[dn][1] = o[dn][2] = o[dn][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  float c[2][4];
+  auto load_q = [&]() {
     const int mat = lane >> 3, r = lane & 7;
 #pragma unroll
     for (int ks = 0; ks < 4; ++ks)
       ldsm_x4(Qs + (size_t)(r + 8 * (mat & 1)) * KS + 16 * ks + 8 * (mat >> 1), qa[ks][0], qa[ks][1], qa[ks][2],
               qa[ks][3]);
-  }
-  float o[8][4];
+  };
+  auto quad_max = [&](float& a, float& b) {
 #pragma unroll
-  for (int dn = 0; dn < 8; ++dn) o[dn][0] = o[dn][1] = o[dn][2] = o[dn][3] = 0.f;
-  float c[8][4];
-  float den0, den1;  // rows g, g + 8
+    for (int x = 1; x <= 2; x <<= 1) {
+      a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, x));
+      b = fmaxf(b, __shfl_xor_sync(0xffffffffu, b, x));
+    }
+  };
   if (SA) {
+    cp_async_wait<0>();
+    __syncthreads();
+    load_q();
     const int nblk = (nk + CA_BLK - 1) / CA_BLK;
-    float m0 = -INFINITY, m1 = -INFINITY;
-    for (int b = 0; b < nblk; ++b) {  // pass 1: the max over all keys
-      scores64(qa, Ks, b * CA_BLK, lane, c);
+    for (int b = 0; b < nblk; ++b) {  // pass 1: the max of the warp's slices
+      const int k0 = b * CA_BLK + 16 * warp;
+      if (k0 >= nk) break;
+      scores16(qa, Ks, k0, lane, c);
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt)
+      for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
-          const bool ok = b * CA_BLK + 8 * nt + 2 * cc + i < nk;
+          const bool ok = k0 + 8 * nt + 2 * cc + i < nk;
           m0 = fmaxf(m0, ok ? c[nt][i] * p.scale : -INFINITY);
           m1 = fmaxf(m1, ok ? c[nt][2 + i] * p.scale : -INFINITY);
         }
     }
-#pragma unroll
-    for (int x = 1; x <= 2; x <<= 1) {
-      m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, x));
-      m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, x));
+    quad_max(m0, m1);
+    if (cc == 0) {
+      st_s[warp][g][0] = m0;
+      st_s[warp][g + 8][0] = m1;
     }
-    float s0 = 0.f, s1 = 0.f;
-    for (int b = 0; b < nblk; ++b) {  // pass 2: P = exp(s - max), rounded to bf16 for P V
-      scores64(qa, Ks, b * CA_BLK, lane, c);
+    __syncthreads();
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt)
+    for (int w = 0; w < ATT_WARPS; ++w) {  // the max over all keys
+      m0 = fmaxf(m0, st_s[w][g][0]);
+      m1 = fmaxf(m1, st_s[w][g + 8][0]);
+    }
+    for (int b = 0; b < nblk; ++b) {  // pass 2: P = bf16(exp(s - max)), P V and the sums
+      const int k0 = b * CA_BLK + 16 * warp;
+      if (k0 >= nk) break;
+      scores16(qa, Ks, k0, lane, c);
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
-          const bool ok = b * CA_BLK + 8 * nt + 2 * cc + i < nk;
+          const bool ok = k0 + 8 * nt + 2 * cc + i < nk;
           const float p0 = ok ? __expf(c[nt][i] * p.scale - m0) : 0.f;
           const float p1 = ok ? __expf(c[nt][2 + i] * p.scale - m1) : 0.f;
-          s0 += p0;
-          s1 += p1;
+          l0 += p0;
+          l1 += p1;
           c[nt][i] = round_bf(p0);
           c[nt][2 + i] = round_bf(p1);
         }
-      pv64(c, Vs, b * CA_BLK, lane, o);
+      pv16(c, Vs, k0, lane, o);
     }
-    den0 = s0;
-    den1 = s1;
   } else {
     const int nblk = (S + CA_BLK - 1) / CA_BLK;
-    float mx0 = -INFINITY, mx1 = -INFINITY;
-    den0 = den1 = 0.f;
     for (int b = 0; b < nblk; ++b) {
       const int buf = b & 1;
-      if (b + 1 < nblk) {  // next block into the other buffer (free: its last reader was block b - 1)
+      cp_async_wait<0>();
+      __syncthreads();  // block b is in shared memory; every warp is done with block b - 1
+      if (b == 0) load_q();
+      if (b + 1 < nblk) {  // the next block into the other buffer (last read in block b - 1)
         const int nb = min(CA_BLK, S - (b + 1) * CA_BLK);
-        __syncwarp();
-        stage((b + 1) * CA_BLK, nb, (buf ^ 1) * CA_BLK, lane, 32);
-        zero_rows((buf ^ 1) * CA_BLK + nb, (buf ^ 1) * CA_BLK + CA_BLK, lane, 32);
+        stage((b + 1) * CA_BLK, nb, (buf ^ 1) * CA_BLK, tid, 32 * ATT_WARPS);
+        zero_rows((buf ^ 1) * CA_BLK + nb, (buf ^ 1) * CA_BLK + CA_BLK, tid, 32 * ATT_WARPS);
         cp_async_commit();
-        cp_async_wait<1>();
-      } else {
-        cp_async_wait<0>();
       }
-      __syncwarp();
-      scores64(qa, Ks, buf * CA_BLK, lane, c);
+      const int kg = b * CA_BLK + 16 * warp;  // global key index of the slice
+      if (kg >= S) continue;                   // warp-uniform
+      scores16(qa, Ks, buf * CA_BLK + 16 * warp, lane, c);
       float bm0 = -INFINITY, bm1 = -INFINITY;
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt)
+      for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
-          const bool ok = b * CA_BLK + 8 * nt + 2 * cc + i < S;
+          const bool ok = kg + 8 * nt + 2 * cc + i < S;
           c[nt][i] = ok ? c[nt][i] * p.scale : -INFINITY;
           c[nt][2 + i] = ok ? c[nt][2 + i] * p.scale : -INFINITY;
           bm0 = fmaxf(bm0, c[nt][i]);
           bm1 = fmaxf(bm1, c[nt][2 + i]);
         }
-#pragma unroll
-      for (int x = 1; x <= 2; x <<= 1) {
-        bm0 = fmaxf(bm0, __shfl_xor_sync(0xffffffffu, bm0, x));
-        bm1 = fmaxf(bm1, __shfl_xor_sync(0xffffffffu, bm1, x));
-      }
-      const float mn0 = fmaxf(mx0, bm0), mn1 = fmaxf(mx1, bm1);
-      const float al0 = __expf(mx0 - mn0), al1 = __expf(mx1 - mn1);  // 0 on the first block
+      quad_max(bm0, bm1);
+      const float mn0 = fmaxf(m0, bm0), mn1 = fmaxf(m1, bm1);
+      const float al0 = __expf(m0 - mn0), al1 = __expf(m1 - mn1);  // 0 on the warp's first slice
       float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt)
+      for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
           const float p0 = __expf(c[nt][i] - mn0), p1 = __expf(c[nt][2 + i] - mn1);
@@ -611,15 +619,10 @@ __global__ void __launch_bounds__(32 * ATT_WARPS) bt_attention(const __grid_cons
           c[nt][i] = round_bf(p0);
           c[nt][2 + i] = round_bf(p1);
         }
-#pragma unroll
-      for (int x = 1; x <= 2; x <<= 1) {
-        s0 += __shfl_xor_sync(0xffffffffu, s0, x);
-        s1 += __shfl_xor_sync(0xffffffffu, s1, x);
-      }
-      den0 = den0 * al0 + s0;
-      den1 = den1 * al1 + s1;
-      mx0 = mn0;
-      mx1 = mn1;
+      l0 = l0 * al0 + s0;
+      l1 = l1 * al1 + s1;
+      m0 = mn0;
+      m1 = mn1;
 #pragma unroll
       for (int dn = 0; dn < 8; ++dn) {
         o[dn][0] *= al0;
@@ -627,24 +630,45 @@ __global__ void __launch_bounds__(32 * ATT_WARPS) bt_attention(const __grid_cons
         o[dn][2] *= al1;
         o[dn][3] *= al1;
       }
-      pv64(c, Vs, buf * CA_BLK, lane, o);
+      pv16(c, Vs, buf * CA_BLK + 16 * warp, lane, o);
     }
   }
-  if (SA) {  // the SA sums are still per lane
+  // merge: each warp's (max, sum) and partial output, then y = sum_w o_w e^(m_w - M) / sum_w l_w e^(m_w - M)
 #pragma unroll
-    for (int x = 1; x <= 2; x <<= 1) {
-      den0 += __shfl_xor_sync(0xffffffffu, den0, x);
-      den1 += __shfl_xor_sync(0xffffffffu, den1, x);
-    }
+  for (int x = 1; x <= 2; x <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, x);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, x);
+  }
+  __syncthreads();  // every warp is done with K / V: the partial outputs go over them
+  float* Op = reinterpret_cast<float*>(Ks);  // [ATT_WARPS][16][OPS]
+  if (cc == 0) {
+    st_s[warp][g][0] = m0;
+    st_s[warp][g][1] = l0;
+    st_s[warp][g + 8][0] = m1;
+    st_s[warp][g + 8][1] = l1;
   }
 #pragma unroll
   for (int dn = 0; dn < 8; ++dn) {
     const int d = 8 * dn + 2 * cc;
-    if (g < T)
-      *reinterpret_cast<uint32_t*>(p.y + ((size_t)e * T + g) * H + h * HD + d) = pack_bf2(o[dn][0] / den0, o[dn][1] / den0);
-    if (g + 8 < T)
-      *reinterpret_cast<uint32_t*>(p.y + ((size_t)e * T + g + 8) * H + h * HD + d) =
-          pack_bf2(o[dn][2] / den1, o[dn][3] / den1);
+    *reinterpret_cast<float2*>(Op + (warp * 16 + g) * OPS + d) = make_float2(o[dn][0], o[dn][1]);
+    *reinterpret_cast<float2*>(Op + (warp * 16 + g + 8) * OPS + d) = make_float2(o[dn][2], o[dn][3]);
+  }
+  __syncthreads();
+  for (int i = tid; i < T * (HD / 2); i += 32 * ATT_WARPS) {  // (row, column pair)
+    const int t = i / (HD / 2), d = 2 * (i % (HD / 2));
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < ATT_WARPS; ++w) M = fmaxf(M, st_s[w][t][0]);
+    float L = 0.f, y0 = 0.f, y1 = 0.f;
+#pragma unroll
+    for (int w = 0; w < ATT_WARPS; ++w) {
+      const float f = __expf(st_s[w][t][0] - M);  // 0 for a warp without keys (max -inf)
+      const float2 v = *reinterpret_cast<const float2*>(Op + (w * 16 + t) * OPS + d);
+      L = fmaf(st_s[w][t][1], f, L);
+      y0 = fmaf(v.x, f, y0);
+      y1 = fmaf(v.y, f, y1);
+    }
+    *reinterpret_cast<uint32_t*>(p.y + ((size_t)e * T + t) * H + h * HD + d) = pack_bf2(y0 / L, y1 / L);
   }
 }
 
