@@ -52,6 +52,44 @@ def ready_value(seq: int) -> int:
     return (seq - 1) % READY_PERIOD + 1
 
 
+def _copy_groups(L: int):
+    """Layer groups of run_from_host's K/V copies, each group followed by its layers' readiness
+    words: single layers first (the launch needs them soonest), larger runs later (fewer copies: each
+    costs the host ~2.5 us to enqueue and the copy engine a fixed overhead; the 10 x 0.79 MB of a
+    predict's K/V then cross at the engine's full rate well inside the first Euler step)."""
+    sizes, out, l = [1, 1, 2, 2], [], 0
+    for n in sizes:
+        if l >= L:
+            break
+        out.append((l, min(L, l + n)))
+        l = min(L, l + n)
+    if l < L:
+        out.append((l, L))
+    return out
+
+
+def _merged(pairs):
+    """(dst, src) copies of consecutive layers, merged where both the device and the host tensors
+    continue each other in memory (one copy instead of several)."""
+    out = []
+    for d, h in pairs:
+        if out:
+            pd, ph = out[-1]
+            if (pd.data_ptr() + pd.numel() * pd.element_size() == d.data_ptr()
+                    and ph.data_ptr() + ph.numel() * ph.element_size() == h.data_ptr()
+                    and pd.dtype == d.dtype and ph.dtype == h.dtype):
+                n = pd.numel() + d.numel()
+                out[-1] = (_flat(pd, n), _flat(ph, n))
+                continue
+        out.append((d, h))
+    return out
+
+
+def _flat(t: torch.Tensor, n: int) -> torch.Tensor:
+    """A 1-D view of n elements starting at t's first element (t contiguous)."""
+    return torch.as_strided(t, (n,), (1,))
+
+
 class ExpertMegakernel:
     """Packs the expert weights once; ``run`` integrates Euler steps 2..N in one launch."""
 
@@ -225,16 +263,25 @@ class ExpertMegakernel:
         st = past.register_step
         host = {"x": x_t, "mods": mods, "sa_cos": st["sa_pe"][0], "sa_sin": st["sa_pe"][1],
                 "ca_cos": st["ca_pe"][0], "ca_sin": st["ca_pe"][1], "cu_kv": st["cu_kv"], "cu_src": st["cu_src"]}
-        if isinstance(dt, torch.Tensor):
-            host["dt"] = dt.reshape(-1)[:1]
         if len(st["mem_kv"]) != self.L or len(past.cross_attn_kv) != self.L:
             raise ValueError("need one memory and one cross-attention K/V pair per layer")
         kv = [(m[0], m[1], c[0], c[1]) for m, c in zip(st["mem_kv"], past.cross_attn_kv)]
-        tensors = list(host.values()) + [x for layer in kv for x in layer]
-        key = tuple((k, tuple(v.shape), v.dtype) for k, v in host.items()) + tuple(
-            (tuple(t.shape), t.dtype) for layer in kv for t in layer)
-        seen = (key, tuple(t.data_ptr() for t in tensors), tuple(t.stride() for t in tensors))
+        objs = tuple(host.values()) + tuple(x for layer in kv for x in layer) + (dt,)
+        last = getattr(self, "_host_last", None)
+        if last is not None and len(last[0]) == len(objs) and all(a is b for a, b in zip(last[0], objs)):
+            # the very tensor objects of the last call (a control loop refilling its pinned buffers):
+            # their shapes, strides and addresses were checked then; only the contents are new
+            host, seen = last[1], last[2]
+        else:
+            if isinstance(dt, torch.Tensor):
+                host["dt"] = dt.reshape(-1)[:1]
+            tensors = list(host.values()) + [x for layer in kv for x in layer]
+            key = tuple((k, tuple(v.shape), v.dtype) for k, v in host.items()) + tuple(
+                (tuple(t.shape), t.dtype) for layer in kv for t in layer)
+            seen = (key, tuple(t.data_ptr() for t in tensors), tuple(t.stride() for t in tensors))
+        self._host_last = None  # set again once this call's checks have passed
         if seen != getattr(self, "_host_seen", None):  # the same host tensors as last call: checked then
+            tensors = list(host.values()) + [x for layer in kv for x in layer]
             storages = {}
             for t in tensors:
                 if t.device.type != "cpu" or not t.is_contiguous():
@@ -243,11 +290,12 @@ class ExpertMegakernel:
             if not all(t.is_pinned() for t in storages.values()):
                 raise ValueError("run_from_host takes tensors in pinned host memory")
             self._host_seen = seen
+        key = seen[0]
         b = getattr(self, "_host_bufs", None)
         if b is None or b["key"] != key:
             b = {"key": key,
                  "in": {k: torch.empty(v.shape, dtype=v.dtype, device=dev) for k, v in host.items()},
-                 "kv": [tuple(torch.empty(t.shape, dtype=t.dtype, device=dev) for t in layer) for layer in kv],
+                 "kv": self._device_kv(kv, dev),
                  "ready": torch.zeros(self.L, dtype=torch.int32, device=dev),
                  "ring": torch.zeros((64, self.L), dtype=torch.int32).pin_memory(),
                  "ring_done": [None] * 64, "seq": 0,
@@ -259,7 +307,20 @@ class ExpertMegakernel:
         main = torch.cuda.current_stream(dev)
         if b["prev"] is not None and b["prev_stream"] != main:
             main.wait_event(b["prev"])  # the previous launch, on another stream, still reads b["in"]
-        self._h2d([(b["in"][k], v) for k, v in host.items()], main)
+        plan = b.get("plan")
+        if plan is None or plan["seen"] != seen:
+            # the copy lists for these host tensors, as library-call arguments built once; the readiness
+            # words' sources (the ring row of the call) are patched in per call
+            side, ready_at = [], []
+            for l0, l1 in _copy_groups(self.L):
+                for j in range(4):  # memory K, V, cross-attention K, V of layers l0..l1-1
+                    side += _merged([(b["kv"][l][j], kv[l][j]) for l in range(l0, l1)])
+                ready_at.append((len(side), l0, l1))
+                side.append((b["ready"][l0:l1], b["ring"][0][l0:l1]))
+            plan = {"seen": seen, "small": self._h2d_args([(b["in"][k], v) for k, v in host.items()]),
+                    "side": self._h2d_args(side), "ready_at": ready_at}
+            b["plan"] = plan
+        self._h2d_run(plan["small"], main)
         b["seq"] += 1
         value = ready_value(b["seq"])
         slot = b["seq"] % 64
@@ -270,11 +331,10 @@ class ExpertMegakernel:
         cs = b["copy"]
         if b["prev"] is not None:
             cs.wait_event(b["prev"])  # the previous launch has finished with the buffers
-        pairs = []
-        for l in range(self.L):
-            pairs += list(zip(b["kv"][l], kv[l]))
-            pairs.append((b["ready"][l:l + 1], row[l:l + 1]))
-        self._h2d(pairs, cs)  # enqueued before the launch: the copies start while it is prepared
+        side = plan["side"]
+        for idx, l0, l1 in plan["ready_at"]:  # this call's ring row
+            side[2][idx] = row[l0:l1].data_ptr()
+        self._h2d_run(side, cs)  # enqueued before the launch: the copies start while it is prepared
         ev = torch.cuda.Event()
         ev.record(cs)
         if b.get("si") is None or b["dt_key"] != (None if "dt" in host else float(dt)):
@@ -305,15 +365,43 @@ class ExpertMegakernel:
         done.record(main)
         b["ring_done"][slot] = ev
         b["prev"], b["prev_stream"] = done, main
+        self._host_last = (objs, host, seen)
         return out
 
-    def _h2d(self, pairs, stream) -> None:
-        """Host-to-device copies (dst, src) in order on `stream`, one library call for all."""
+    @staticmethod
+    def _device_kv(kv, dev):
+        """Device K/V buffers for run_from_host: per kind (memory K, V, cross-attention K, V) one
+        allocation holding every layer back to back, so a run of layers can be one copy."""
+        out = [[None] * 4 for _ in kv]
+        for j in range(4):
+            shapes = [tuple(layer[j].shape) for layer in kv]
+            dt = kv[0][j].dtype
+            if all(sh == shapes[0] for sh in shapes) and all(layer[j].dtype == dt for layer in kv):
+                whole = torch.empty((len(kv),) + shapes[0], dtype=dt, device=dev)
+                for l in range(len(kv)):
+                    out[l][j] = whole[l]
+            else:
+                for l, layer in enumerate(kv):
+                    out[l][j] = torch.empty(layer[j].shape, dtype=layer[j].dtype, device=dev)
+        return [tuple(o) for o in out]
+
+    @staticmethod
+    def _h2d_args(pairs):
+        """(n, dst, src, bytes) library-call arguments of host-to-device copies (dst, src)."""
         n = len(pairs)
         dst = (C.c_void_p * n)(*[dd.data_ptr() for dd, _ in pairs])
         src = (C.c_void_p * n)(*[ss.data_ptr() for _, ss in pairs])
         nb = (C.c_size_t * n)(*[ss.numel() * ss.element_size() for _, ss in pairs])
+        return [n, dst, src, nb]
+
+    def _h2d_run(self, args, stream) -> None:
+        """The copies of `args` (from _h2d_args) in order on `stream`, one library call for all."""
+        n, dst, src, nb = args
         _lib.check(self._lib.mkx_h2d_copies(n, dst, src, nb, C.c_void_p(stream.cuda_stream)), "mkx_h2d_copies")
+
+    def _h2d(self, pairs, stream) -> None:
+        """Host-to-device copies (dst, src) in order on `stream`, one library call for all."""
+        self._h2d_run(self._h2d_args(pairs), stream)
 
     def barriers(self, n_steps: int) -> int:
         return int(self._lib.mkx_sync_points(self._h, int(n_steps)))
