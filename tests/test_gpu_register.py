@@ -115,7 +115,7 @@ def test_register_pass_rejects_bad_arguments(parts):
         bx.register_pass(*args(torch.zeros((32, d.H), dtype=torch.bfloat16)))                  # host tensor
 
 
-def _predictors(d, w, bx, S, graph=True):
+def _predictors(d, w, bx, S, graph=True, T=10, frames=3):
     from reki_megakernel_b200.full_predict import FullPredict
     from reki_megakernel_b200.mk_expert import ExpertMegakernel
     from reki_megakernel_b200.modulations import StepModulations
@@ -123,14 +123,15 @@ def _predictors(d, w, bx, S, graph=True):
     mk = ExpertMegakernel(weights=w.to(DEV))
     rp = RegisterPrepare(make_prepare_weights(d, seed=0).to(DEV))
     sm = StepModulations(make_modulation_weights(d, seed=0).to(DEV))
-    fp = FullPredict(mk, bx, rp, sm, make_register_rows(d, 32).to(DEV), S=S, num_steps=10, T=10, graph=graph)
+    fp = FullPredict(mk, bx, rp, sm, make_register_rows(d, 32).to(DEV), S=S, num_steps=10, T=T, frames=frames,
+                     graph=graph)
     return fp, (mk, rp, sm)
 
 
-def _predict_inputs(d, p, S, sdim=7):
+def _predict_inputs(d, p, S, sdim=7, T=10):
     src = make_source(S, d.src_dim, seed=100 + p)
     state = make_state(sdim, seed=100 + p)
-    noise = torch.randn((1, 10, d.A), generator=torch.Generator().manual_seed(1234 + p))
+    noise = torch.randn((1, T, d.A), generator=torch.Generator().manual_seed(1234 + p))
     return src, state, noise
 
 
@@ -210,3 +211,26 @@ def test_graph_replays_equal_eager_predicts(parts):
     torch.cuda.synchronize()
     assert torch.equal(again, ref0)
     assert not torch.equal(first, again)  # the 5th predict saw three frames of memory
+
+
+@pytest.mark.parametrize("S,T,frames", [(1, 10, 3), (300, 16, 2), (64, 1, 1)])
+def test_carried_predict_shapes(parts, S, T, frames):
+    """Source lengths 1 and 300, 16 and 1 action rows, 2 frames and a single frame (kv_start 0 from
+    the first predict, nothing carried): 5 predicts each against the restatement."""
+    from oracle.register_oracle import PredictOracle
+    name, d, w, bx, orc, orc32 = parts
+    if name != "small":
+        pytest.skip("small expert only")
+    fp, keep = _predictors(d, w, bx, S, T=T, frames=frames)
+    po = PredictOracle(orc, make_prepare_weights(d, seed=0), make_modulation_weights(d, seed=0),
+                       make_register_rows(d, 32), N=10, PM=32 * frames, R=32, T=T, action_dim=7)
+    for p in range(5):
+        src, state, noise = _predict_inputs(d, p, S, T=T)
+        got = fp(src.to(DEV), state.to(DEV), noise.to(DEV)).clone()
+        torch.cuda.synchronize()
+        fp.check_device_errors()
+        ref = po.predict(src, state, noise[0], kv=(fp.k, fp.v), mods_dt=(fp.mods[1:], fp.dt.item()))
+        mx, mean = chunk_err(got[0], ref, 7)
+        assert torch.isfinite(got).all()
+        assert mx <= TOL_MAX and mean <= TOL_MEAN, (S, T, frames, p, mx, mean)
+
