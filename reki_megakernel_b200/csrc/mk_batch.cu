@@ -433,6 +433,7 @@ struct AttnParams {
   int T;
   int kcap;              // SA: key rows of the shared K / V tiles (PM + T rounded up to 64)
   int own;               // SA: 1 the query rows' own keys follow the memory rows; 0 memory rows only
+  int kv_input;          // 1: K / V and lim were in memory before the launch sequence (staged early)
   int lim_stride;        // episode stride of lim (0: one value for all episodes)
   float qk_eps, scale;
 };
@@ -442,9 +443,10 @@ constexpr int OPS = HD + 4;  // floats per row of a warp's partial attention out
 
 template <bool SA>
 __global__ void __launch_bounds__(32 * ATT_WARPS) bt_attention(const __grid_constant__ AttnParams p) {
-  grid_dep_wait();
+  // K / V (and the row limits) that were in memory before the launch sequence began are staged before
+  // waiting for the previous kernel; K / V a kernel of the sequence writes, after
+  if (!p.kv_input) grid_dep_wait();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, cc = lane & 3, T = p.T;
-  if (tid == 0) grid_dep_launch();
   extern __shared__ __align__(16) char asmem[];
   __shared__ float st_s[ATT_WARPS][16][2];  // per warp and query row: softmax max, sum
   const int e = blockIdx.x / NH, h = blockIdx.x % NH;
@@ -483,6 +485,8 @@ __global__ void __launch_bounds__(32 * ATT_WARPS) bt_attention(const __grid_cons
     zero_rows(nb, CA_BLK, tid, 32 * ATT_WARPS);
   }
   cp_async_commit();
+  if (p.kv_input) grid_dep_wait();  // the queries are the previous kernel's output
+  if (tid == 0) grid_dep_launch();
   // queries (and SA own keys / values), bf16, rows >= T zero: warp w takes rows w, w + 4, ...
   for (int t = warp; t < 16; t += ATT_WARPS) {
     uint32_t qv = 0u;
@@ -1138,6 +1142,7 @@ struct LayerIO {
   int ca_rows;
   const int* src_rows;
   int lim_stride, own;
+  int sa_input, ca_input;  // memory / cross-attention K/V written before the sequence (bt_attention kv_input)
   const float *sa_cos, *sa_sin, *ca_cos, *ca_sin;
   int frame_row0;  // < 0: no frame to write
 };
@@ -1179,6 +1184,7 @@ void seq_layer(Seq& q, int l, const uint16_t* blk, const LayerIO& io) {
   ap.wk = h->nrm + (size_t)(L + l) * HD;
   ap.kcap = kcap;
   ap.own = io.own;
+  ap.kv_input = io.sa_input;
   if (q.err == cudaSuccess && q.st == MKX_OK)
     q.err = launch_pdl(bt_attention<true>, dim3(q.B * NH), dim3(32 * ATT_WARPS), att_sa, q.stream, ap);
   seq_gemm(q, G_O, l, 1, h->h, H, blk + 2 * H);
@@ -1196,6 +1202,7 @@ void seq_layer(Seq& q, int l, const uint16_t* blk, const LayerIO& io) {
   ap.sin = io.ca_sin;
   ap.wq = h->nrm + (size_t)(2 * L + l) * HD;
   ap.wk = nullptr;
+  ap.kv_input = io.ca_input;
   if (q.err == cudaSuccess && q.st == MKX_OK)
     q.err = launch_pdl(bt_attention<false>, dim3(q.B * NH), dim3(32 * ATT_WARPS), att_ca, q.stream, ap);
   seq_gemm(q, G_OCA, l, 1, h->h, H, blk + 5 * H);
@@ -1251,6 +1258,8 @@ extern "C" mkx_status mkx_batch_run(mkx_batch_handle* h, const mkx_batch_inputs*
   io.src_rows = in->src_rows;
   io.lim_stride = 1;
   io.own = 1;
+  io.sa_input = 1;  // the caller's memory and cross-attention K/V
+  io.ca_input = 1;
   io.sa_cos = in->sa_cos;
   io.sa_sin = in->sa_sin;
   io.ca_cos = in->ca_cos;
@@ -1323,6 +1332,8 @@ extern "C" mkx_status mkx_batch_register_pass(mkx_batch_handle* h, const mkx_reg
   io.src_rows = in->src_rows;
   io.lim_stride = 0;
   io.own = 0;
+  io.sa_input = 0;  // the frame's rows are written by the pass itself
+  io.ca_input = 1;
   io.sa_cos = in->sa_cos;
   io.sa_sin = in->sa_sin;
   io.ca_cos = in->ca_cos;
