@@ -354,6 +354,8 @@ __global__ void __launch_bounds__(256) bt_adarms(const uint16_t* __restrict__ h,
 // ---------------------------------------------------------------------------------------------
 constexpr int SA_MAXK = 320;          // memory rows + own rows (<= 256 + 16), whole 64-key blocks
 constexpr int CA_BLK = 64;
+constexpr int CA_ALL_ROWS = 3 * CA_BLK;  // padded source rows up to which CA stages all of them at once
+constexpr int CA_ALL_UNITS_PER_SM = 4;     // ... while there are at most this many (episode, head) units per SM
 constexpr int KS = 72;                // shared row stride (bf16) of the Q / K / V tiles: ldmatrix rows of
                                       // 144 bytes fall in distinct bank quadruples
 
@@ -431,9 +433,11 @@ struct AttnParams {
   const float* wq;       // [HD] 1 + q norm weight (SA q / CA q)
   const float* wk;       // [HD] 1 + k norm weight (SA own keys)
   int T;
-  int kcap;              // SA: key rows of the shared K / V tiles (PM + T rounded up to 64)
+  int kcap;              // key rows of the shared K / V tiles: SA PM + T rounded up to 64; CA 2 blocks, or
+                         // the whole padded source (ca_all) when it has at most CA_ALL_ROWS rows
   int own;               // SA: 1 the query rows' own keys follow the memory rows; 0 memory rows only
   int kv_input;          // 1: K / V and lim were in memory before the launch sequence (staged early)
+  int ca_all;            // CA: 1 = the whole padded source (kcap rows) staged at once
   int lim_stride;        // episode stride of lim (0: one value for all episodes)
   float qk_eps, scale;
 };
@@ -452,7 +456,9 @@ __global__ void __launch_bounds__(32 * ATT_WARPS) bt_attention(const __grid_cons
   const int e = blockIdx.x / NH, h = blockIdx.x % NH;
   uint16_t* Qs = reinterpret_cast<uint16_t*>(asmem);             // [16][KS]
   uint16_t* Ks = Qs + 16 * KS;                                    // SA: [SA_MAXK][KS]; CA: [2][64][KS]
-  uint16_t* Vs = Ks + (SA ? p.kcap : 2 * CA_BLK) * KS;
+  // CA with kcap > 2 blocks: every source row staged at once (no double buffering)
+  const bool ca_all = !SA && p.ca_all;
+  uint16_t* Vs = Ks + ((SA || ca_all) ? p.kcap : 2 * CA_BLK) * KS;
   const uint16_t* kb = p.kb + (size_t)e * p.kv_ep + h * HD;
   const uint16_t* vb = p.vb + (size_t)e * p.kv_ep + h * HD;
   const uint32_t zero = 0u;
@@ -480,9 +486,9 @@ __global__ void __launch_bounds__(32 * ATT_WARPS) bt_attention(const __grid_cons
     zero_rows(nk, (nk + CA_BLK - 1) / CA_BLK * CA_BLK, tid, 32 * ATT_WARPS);
   } else {
     S = min(max(p.lim[e * p.lim_stride], 1), p.kv_rows);
-    const int nb = min(CA_BLK, S);
+    const int nb = ca_all ? S : min(CA_BLK, S);
     stage(0, nb, 0, tid, 32 * ATT_WARPS);
-    zero_rows(nb, CA_BLK, tid, 32 * ATT_WARPS);
+    zero_rows(nb, ca_all ? (S + CA_BLK - 1) / CA_BLK * CA_BLK : CA_BLK, tid, 32 * ATT_WARPS);
   }
   cp_async_commit();
   if (p.kv_input) grid_dep_wait();  // the queries are the previous kernel's output
@@ -585,11 +591,11 @@ __global__ void __launch_bounds__(32 * ATT_WARPS) bt_attention(const __grid_cons
   } else {
     const int nblk = (S + CA_BLK - 1) / CA_BLK;
     for (int b = 0; b < nblk; ++b) {
-      const int buf = b & 1;
+      const int buf = ca_all ? b : b & 1;  // shared block of block b
       cp_async_wait<0>();
       __syncthreads();  // block b is in shared memory; every warp is done with block b - 1
       if (b == 0) load_q();
-      if (b + 1 < nblk) {  // the next block into the other buffer (last read in block b - 1)
+      if (!ca_all && b + 1 < nblk) {  // the next block into the other buffer (last read in block b - 1)
         const int nb = min(CA_BLK, S - (b + 1) * CA_BLK);
         stage((b + 1) * CA_BLK, nb, (buf ^ 1) * CA_BLK, tid, 32 * ATT_WARPS);
         zero_rows((buf ^ 1) * CA_BLK + nb, (buf ^ 1) * CA_BLK + CA_BLK, tid, 32 * ATT_WARPS);
@@ -1154,7 +1160,12 @@ void seq_layer(Seq& q, int l, const uint16_t* blk, const LayerIO& io) {
   const int L = h->d.L, I = h->d.I;
   const int kcap = (io.mem_rows + (io.own ? q.T : 0) + CA_BLK - 1) / CA_BLK * CA_BLK;  // <= SA_MAXK
   const size_t att_sa = (size_t)(16 + 2 * kcap) * KS * 2;
-  const size_t att_ca = (size_t)(16 + 4 * CA_BLK) * KS * 2;
+  // cross-attention: the whole padded source at once when it fits 3 blocks and the (episode, head)
+  // units are few (one round of copies in flight per CTA); with many units, 2 blocks double-buffered
+  // (smaller CTAs, more of them per SM)
+  const bool ca_all = io.ca_rows <= CA_ALL_ROWS && q.B * NH <= CA_ALL_UNITS_PER_SM * h->sms;
+  const int ca_cap = ca_all ? (io.ca_rows + CA_BLK - 1) / CA_BLK * CA_BLK : 2 * CA_BLK;
+  const size_t att_ca = (size_t)(16 + 2 * ca_cap) * KS * 2;
   const uint16_t* memk_l = io.memk + (size_t)l * io.mem_rows * H;
   const uint16_t* memv_l = io.memv + (size_t)l * io.mem_rows * H;
   AttnParams ap;
@@ -1203,6 +1214,8 @@ void seq_layer(Seq& q, int l, const uint16_t* blk, const LayerIO& io) {
   ap.wq = h->nrm + (size_t)(2 * L + l) * HD;
   ap.wk = nullptr;
   ap.kv_input = io.ca_input;
+  ap.kcap = ca_cap;
+  ap.ca_all = ca_all ? 1 : 0;
   if (q.err == cudaSuccess && q.st == MKX_OK)
     q.err = launch_pdl(bt_attention<false>, dim3(q.B * NH), dim3(32 * ATT_WARPS), att_ca, q.stream, ap);
   seq_gemm(q, G_OCA, l, 1, h->h, H, blk + 5 * H);
