@@ -307,10 +307,19 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) bt_gemm(const __grid_constant
 __global__ void __launch_bounds__(256) bt_adarms(const uint16_t* __restrict__ h, uint16_t* __restrict__ a, int M, int Mp,
                                                  int T, const uint16_t* __restrict__ mods_blk, long long ep_stride,
                                                  float eps) {
-  grid_dep_wait();
-  if (threadIdx.x == 0) grid_dep_launch();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * 8 + warp;
+  uint4 v[3], s4[3], h4[3];
+  if (row < M) {  // the modulation rows are inputs of the launch sequence: read before the wait
+    const uint16_t* sc = mods_blk + (size_t)(row / T) * ep_stride;
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+      s4[i] = __ldg(reinterpret_cast<const uint4*>(sc) + lane + 32 * i);
+      h4[i] = __ldg(reinterpret_cast<const uint4*>(sc + H) + lane + 32 * i);
+    }
+  }
+  grid_dep_wait();
+  if (threadIdx.x == 0) grid_dep_launch();
   if (row >= Mp) return;
   uint4* dst = reinterpret_cast<uint4*>(a + (size_t)row * H);
   if (row >= M) {
@@ -319,14 +328,8 @@ __global__ void __launch_bounds__(256) bt_adarms(const uint16_t* __restrict__ h,
     return;
   }
   const uint4* src = reinterpret_cast<const uint4*>(h + (size_t)row * H);
-  const uint16_t* sc = mods_blk + (size_t)(row / T) * ep_stride;
-  uint4 v[3], s4[3], h4[3];
 #pragma unroll
-  for (int i = 0; i < 3; ++i) {  // every load first: one memory latency for the row
-    v[i] = src[lane + 32 * i];
-    s4[i] = __ldg(reinterpret_cast<const uint4*>(sc) + lane + 32 * i);
-    h4[i] = __ldg(reinterpret_cast<const uint4*>(sc + H) + lane + 32 * i);
-  }
+  for (int i = 0; i < 3; ++i) v[i] = src[lane + 32 * i];
   float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < 3; ++i) {
