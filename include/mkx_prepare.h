@@ -48,7 +48,7 @@ mkx_status mkx_prep_create(const mkx_prep_dims* dims, const uint16_t* wkv, const
                            mkx_prep_handle** out);
 
 /* src: [S][src_dim] bf16, 16-byte aligned rows; cos, sin: [S][HD] fp32 RoPE tables of the source
- * positions; k_out, v_out: [L][SP][NH][HD] bf16 with SP >= S (rows S..SP-1 are not written).
+ * positions, 16-byte aligned (MKX_ERR_INVALID_ARG otherwise, as for src, k_out and v_out); k_out, v_out: [L][SP][NH][HD] bf16 with SP >= S (rows S..SP-1 are not written).
  * 1 <= S <= 4096. Asynchronous on `stream`; graph-capturable. A device-side wait that runs out of
  * time sets the error word (mkx_prep_last_error) and the launch returns without hanging. */
 mkx_status mkx_prep_run(mkx_prep_handle* h, const uint16_t* src, int S, const float* cos, const float* sin,

@@ -4,16 +4,19 @@
 //   D[f, n] = sum_k Wkv[f, k] * src[n, k]      f over [L][K|V][768] (15,360 rows at REKI's sizes)
 //
 // One CTA per (128-feature tile, block of <= 256 tokens). Warp 0: producer into an mbarrier ring of up
-// to 8 stages: the W tile as one contiguous 16 KB bulk copy from a copy of W packed at create time in
-// the 128-byte-swizzled K-major order the MMA reads (tile-contiguous, so HBM sees long bursts), the
-// source rows by TMA with the same swizzle. Warp 1: allocates 256 TMEM columns and issues
-// tcgen05.mma kind::f16 (M = 128, N = tokens, K = 16 per instruction, bf16 in, fp32 accumulate in
-// TMEM), committing each stage back to the producer. Warps 2-5 (one per TMEM lane quarter): read the
-// accumulator with tcgen05.ld, transpose it through shared memory (reusing the drained stage ring);
-// then all 12 warps, per token, apply the K head RMSNorm (1 + kn) and rotate-half RoPE in fp32,
-// round once to bf16 and store rows of the [L][SP][NH][HD] outputs (12 warps: the K tiles' norm and
-// RoPE, with their table loads, took 5.4 us after a 14.8 us mainloop with 6). Every wait is bounded by %globaltimer; after a
-// timeout the CTA records the error, drains its copies and MMAs, frees TMEM and returns.
+// to 8 stages (the first ring of copies goes out right after the barriers are initialised, before
+// the TMEM allocation): the W tile as one contiguous 16 KB bulk copy from a copy of W packed at create
+// time in the 128-byte-swizzled K-major order the MMA reads (tile-contiguous, so HBM sees long
+// bursts), the source rows by TMA with the same swizzle. Warp 1: allocates 256 TMEM columns and
+// issues tcgen05.mma kind::f16 (M = 128, N = tokens, K = 16 per instruction, bf16 in, fp32
+// accumulate in TMEM), committing each stage back to the producer. Warps 2-5 (one per TMEM lane
+// quarter): read the accumulator with tcgen05.ld and transpose it through shared memory (reusing the
+// drained stage ring). Then all 12 warps: in K tiles, one (token, head) row per thread for the head
+// RMSNorm (1 + kn), written back in place; then, per lane, an 8-feature part of a token's rows of
+// both heads: rotate-half RoPE in fp32 (partner dims from a shuffle, the RoPE rows loaded into a
+// register ring ahead of time), one bf16 rounding, coalesced 16-byte stores of the [L][SP][NH][HD]
+// outputs. Every wait is bounded by %globaltimer; after a timeout the CTA records the error, drains
+// its copies and MMAs, frees TMEM and returns.
 #include <cstdint>
 #include <cstring>
 #include <new>
@@ -79,7 +82,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   uint64_t* done = bars + 2 * MAX_STAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * MAX_STAGES + 1);
   int* consumed_slot = reinterpret_cast<int*>(tmem_slot + 1);
+  float* kn_s = reinterpret_cast<float*>(bars + 2 * MAX_STAGES + 4);  // [HD] K norm weights of the layer
 
+  int issued = 0;  // producer (thread 0): k tiles whose copies have been issued
+  auto issue = [&](int kb) {
+    const int s = kb % STAGES;
+    char* a = ring + s * stage_bytes;
+    mbar_expect_tx(&full[s], (uint32_t)stage_bytes);
+    bulk_g2s(a, p.wpk + ((size_t)tile * p.ktiles + kb) * (A_BYTES / 2), (uint32_t)A_BYTES, &full[s]);
+    tma_load_2d(a + A_BYTES, &ts, kb * BK, tok0, &full[s]);
+    issued = kb + 1;
+  };
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
@@ -88,26 +101,34 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     mbar_init(done, 1);
     *consumed_slot = 0;
     fence_mbar_init();
+    // the first ring of copies needs only these barriers: it goes out before the TMEM allocation and
+    // the block barrier
+    for (int kb = 0; kb < min(STAGES, p.ktiles); ++kb) issue(kb);
   }
   if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+  if (warp == 3 && lane < HD / 4)
+    reinterpret_cast<float4*>(kn_s)[lane] =
+        __ldg(reinterpret_cast<const float4*>(p.kn + (size_t)(tile / TILES_PER_LAYER) * HD) + lane);
+  if (threadIdx.x == 64 && tile % TILES_PER_LAYER < TILES_PER_LAYER / 2) {
+    // K tiles: the RoPE rows of this CTA's tokens are read only at the end; asking L2 for them now
+    // takes their HBM latency off the epilogue
+    const int nv = min(p.ntok, p.S - tok0);
+    bulk_prefetch_l2(p.cos + (size_t)tok0 * HD, (uint32_t)(nv * HD * 4));
+    bulk_prefetch_l2(p.sin + (size_t)tok0 * HD, (uint32_t)(nv * HD * 4));
+  }
   __syncthreads();
   tmem_fence_after();
   const uint32_t tmem = *tmem_slot;
-  int issued = 0;
 
   if (warp == 0 && lane == 0) {
     // producer
-    for (int kb = 0; kb < p.ktiles; ++kb) {
+    for (int kb = issued; kb < p.ktiles; ++kb) {
       const int s = kb % STAGES;
-      if (kb >= STAGES && !wait_bounded(&empty[s], ((kb / STAGES) & 1) ^ 1, p.timeout_ns)) {
+      if (!wait_bounded(&empty[s], ((kb / STAGES) & 1) ^ 1, p.timeout_ns)) {
         record(p, 0x100 | 1);
         break;
       }
-      char* a = ring + s * stage_bytes;
-      mbar_expect_tx(&full[s], (uint32_t)stage_bytes);
-      bulk_g2s(a, p.wpk + ((size_t)tile * p.ktiles + kb) * (A_BYTES / 2), (uint32_t)A_BYTES, &full[s]);
-      tma_load_2d(a + A_BYTES, &ts, kb * BK, tok0, &full[s]);
-      issued = kb + 1;
+      issue(kb);
     }
   } else if (warp == 1 && lane == 0) {
     // MMA issuer
@@ -148,69 +169,104 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     tmem_fence_before();
   }
+  const int l = tile / TILES_PER_LAYER, within = tile % TILES_PER_LAYER;
+  const bool is_k = within < TILES_PER_LAYER / 2;
+  const int h0 = 2 * (within % (TILES_PER_LAYER / 2));
+  const int nvalid = min(p.ntok, p.S - tok0);
+  const int nch = 8 * nvalid, part = lane & 7;
+  const int iters = nch > 32 * warp ? (nch - 32 * warp + NTHREADS - 1) / NTHREADS : 0;  // warp-uniform
+  const float* cosb = p.cos + (size_t)tok0 * HD + 8 * part;
+  const float* sinb = p.sin + (size_t)tok0 * HD + 8 * part;
+  constexpr int RS = 4;  // RoPE ring slots
+  float4 tb[RS][4];
+  auto tload = [&](int i, float4 (&t)[4]) {
+    const int c = 32 * warp + lane + i * NTHREADS;
+    const size_t off = (size_t)(c < nch ? c >> 3 : 0) * HD;
+    t[0] = __ldg(reinterpret_cast<const float4*>(cosb + off));
+    t[1] = __ldg(reinterpret_cast<const float4*>(cosb + off) + 1);
+    t[2] = __ldg(reinterpret_cast<const float4*>(sinb + off));
+    t[3] = __ldg(reinterpret_cast<const float4*>(sinb + off) + 1);
+  };
+  if (is_k) {  // the RoPE ring's first loads go out before the barrier (global reads only)
+#pragma unroll
+    for (int u = 0; u < RS; ++u)
+      if (u < iters) tload(u, tb[u]);
+  }
   ok = __syncthreads_and(ok);  // all roles done; the tile is complete (or a wait failed)
-  // Epilogue, part 2 (all 12 warps): one (token, head) row per half-warp; lane j holds dims 4j..4j+3.
-  // K: head RMSNorm (shuffle reduction over the 16 lanes) * (1 + kn), rotate-half RoPE (partner dims
-  // d +- 32 sit in lane j ^ 8); V: as is. One bf16 rounding, 8-byte stores (128 B per row).
-  if (ok) {
-    const int l = tile / TILES_PER_LAYER, within = tile % TILES_PER_LAYER;
-    const bool is_k = within < TILES_PER_LAYER / 2;
-    const int h0 = 2 * (within % (TILES_PER_LAYER / 2));
-    uint16_t* out = is_k ? p.k_out : p.v_out;
-    const int half = lane >> 4, j = lane & 15;
-    const float4 kn = __ldg(reinterpret_cast<const float4*>(p.kn + (size_t)l * HD) + j);
-    const int nvalid = min(p.ntok, p.S - tok0);
-    const int nitems = 2 * nvalid, nw = NTHREADS / 32;
-    // item = 2 * token + head half; each warp takes two consecutive items per round
-    auto tables = [&](int it, float4& c, float4& sn) {
-      if (is_k && it < nitems) {
-        const size_t n = (size_t)(tok0 + (it >> 1));
-        c = __ldg(reinterpret_cast<const float4*>(p.cos + n * HD) + j);
-        sn = __ldg(reinterpret_cast<const float4*>(p.sin + n * HD) + j);
+  // Epilogue, part 2 (all 12 warps), in two passes over the transposed tile.
+  // (a) K tiles: one (token, head) row of 64 features per thread, items taken head-major (consecutive
+  //     threads read consecutive tokens' rows: no bank conflicts): head RMSNorm * (1 + kn) in fp32,
+  //     the sum of squares formed in the order of a 16-lane butterfly over groups of 4 dims; the
+  //     thread reads its row again and writes it back normalised (kn staged in shared memory).
+  // (b) all tiles, after a barrier: one 8-feature part of a token's rows of both heads per lane, a
+  //     warp covering four tokens' contiguous 256-byte (2 heads) output segments. K: rotate-half RoPE
+  //     in fp32, the partner dims d +- 32 from lane ^ 4, the RoPE rows read from global memory
+  //     (coalesced, once for both heads) into a 4-slot register ring whose first loads go out before
+  //     the transposition barrier, so their L2 latency overlaps pass (a); V: as is. One bf16
+  //     rounding, 16-byte stores.
+  if (ok && is_k) {
+    const float4* kn4 = reinterpret_cast<const float4*>(kn_s);
+    for (int it = threadIdx.x; it < 2 * nvalid; it += NTHREADS) {
+      const int hh = it >= nvalid ? 1 : 0, nl = it - hh * nvalid;
+      float4* row = reinterpret_cast<float4*>(tsm + nl * TS + 64 * hh);
+      float s[16];
+#pragma unroll
+      for (int g = 0; g < 16; ++g) {
+        const float4 y = row[g];
+        s[g] = fmaf(y.x, y.x, fmaf(y.y, y.y, fmaf(y.z, y.z, y.w * y.w)));
       }
-    };
-    // rounds of this warp: items 2 * warp + half + 2 * nw * r; the cos/sin rows of round r + PF are
-    // loaded while round r is processed (an L2 round trip spans several rounds)
-    constexpr int PF = 8;
-    const int rounds = nitems > 2 * warp ? (nitems - 2 * warp + 2 * nw - 1) / (2 * nw) : 0;
-    const int it0 = 2 * warp + half;
-    float4 c[PF], sn[PF];
 #pragma unroll
-    for (int u = 0; u < PF; ++u) {
-      c[u] = sn[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-      tables(it0 + 2 * nw * u, c[u], sn[u]);
+      for (int g = 0; g < 8; ++g) s[g] += s[g + 8];
+#pragma unroll
+      for (int g = 0; g < 4; ++g) s[g] += s[g + 4];
+#pragma unroll
+      for (int g = 0; g < 2; ++g) s[g] += s[g + 2];
+      const float rstd = rsqrtf((s[0] + s[1]) / (float)HD + p.eps);
+#pragma unroll
+      for (int g = 0; g < 16; ++g) {  // the row is the thread's own: read it again, normalise in place
+        const float4 k4 = kn4[g];
+        float4 y = row[g];
+        y.x = y.x * rstd * (1.f + k4.x);
+        y.y = y.y * rstd * (1.f + k4.y);
+        y.z = y.z * rstd * (1.f + k4.z);
+        y.w = y.w * rstd * (1.f + k4.w);
+        row[g] = y;
+      }
     }
-    for (int r0 = 0; r0 < rounds; r0 += PF) {
+  }
+  __syncthreads();
+  if (ok) {
+    uint16_t* out = is_k ? p.k_out : p.v_out;
+    const float sg = part < 4 ? -1.f : 1.f;  // rot[d] = -y[d + 32] for d < 32, y[d - 32] above
+    for (int i0 = 0; i0 < iters; i0 += RS) {
 #pragma unroll
-      for (int u = 0; u < PF; ++u) {
-        const int r = r0 + u;
-        if (r >= rounds) break;  // warp-uniform: the shuffles need all lanes
-        const int it = it0 + 2 * nw * r;
-        const bool valid = it < nitems;
-        const int nl = it >> 1, hh = it & 1;
-        float4 y = valid ? *reinterpret_cast<const float4*>(tsm + nl * TS + 64 * hh + 4 * j)
-                         : make_float4(0.f, 0.f, 0.f, 0.f);
-        if (is_k) {
-          float ss = fmaf(y.x, y.x, fmaf(y.y, y.y, fmaf(y.z, y.z, y.w * y.w)));
+      for (int u = 0; u < RS; ++u) {
+        const int i = i0 + u;
+        if (i >= iters) break;  // warp-uniform: the shuffles need all lanes
+        const int c = 32 * warp + lane + i * NTHREADS;
+        const bool valid = c < nch;
+        const int nl = valid ? c >> 3 : 0;
+        uint16_t* dst = out + (((size_t)l * p.SP + tok0 + nl) * NH + h0) * HD + 8 * part;
 #pragma unroll
-          for (int o = 8; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-          const float rstd = rsqrtf(ss / (float)HD + p.eps);
-          y.x = y.x * rstd * (1.f + kn.x);
-          y.y = y.y * rstd * (1.f + kn.y);
-          y.z = y.z * rstd * (1.f + kn.z);
-          y.w = y.w * rstd * (1.f + kn.w);
-          const float sg = j < 8 ? -1.f : 1.f;  // rot[d] = -y[d + 32] for d < 32, y[d - 32] above
-          const float px = __shfl_xor_sync(0xffffffffu, y.x, 8), py = __shfl_xor_sync(0xffffffffu, y.y, 8);
-          const float pz = __shfl_xor_sync(0xffffffffu, y.z, 8), pw = __shfl_xor_sync(0xffffffffu, y.w, 8);
-          const float4 cc = c[u], ss4 = sn[u];
-          y = make_float4(fmaf(y.x, cc.x, sg * px * ss4.x), fmaf(y.y, cc.y, sg * py * ss4.y),
-                          fmaf(y.z, cc.z, sg * pz * ss4.z), fmaf(y.w, cc.w, sg * pw * ss4.w));
-          tables(it + 2 * nw * PF, c[u], sn[u]);
+        for (int hh = 0; hh < 2; ++hh) {
+          const float4* src = reinterpret_cast<const float4*>(tsm + nl * TS + 64 * hh + 8 * part);
+          float4 a = src[0], b = src[1];
+          if (is_k) {
+            const float4 c0v = tb[u][0], c1v = tb[u][1], s0v = tb[u][2], s1v = tb[u][3];
+            const float pa0 = __shfl_xor_sync(0xffffffffu, a.x, 4), pa1 = __shfl_xor_sync(0xffffffffu, a.y, 4);
+            const float pa2 = __shfl_xor_sync(0xffffffffu, a.z, 4), pa3 = __shfl_xor_sync(0xffffffffu, a.w, 4);
+            const float pb0 = __shfl_xor_sync(0xffffffffu, b.x, 4), pb1 = __shfl_xor_sync(0xffffffffu, b.y, 4);
+            const float pb2 = __shfl_xor_sync(0xffffffffu, b.z, 4), pb3 = __shfl_xor_sync(0xffffffffu, b.w, 4);
+            a = make_float4(fmaf(a.x, c0v.x, sg * pa0 * s0v.x), fmaf(a.y, c0v.y, sg * pa1 * s0v.y),
+                            fmaf(a.z, c0v.z, sg * pa2 * s0v.z), fmaf(a.w, c0v.w, sg * pa3 * s0v.w));
+            b = make_float4(fmaf(b.x, c1v.x, sg * pb0 * s1v.x), fmaf(b.y, c1v.y, sg * pb1 * s1v.y),
+                            fmaf(b.z, c1v.z, sg * pb2 * s1v.z), fmaf(b.w, c1v.w, sg * pb3 * s1v.w));
+          }
+          if (valid)
+            *reinterpret_cast<uint4*>(dst + hh * HD) =
+                make_uint4(pack_bf2(a.x, a.y), pack_bf2(a.z, a.w), pack_bf2(b.x, b.y), pack_bf2(b.z, b.w));
         }
-        if (valid) {
-          uint2* dst = reinterpret_cast<uint2*>(out + (((size_t)l * p.SP + tok0 + nl) * NH + h0 + hh) * HD) + j;
-          *dst = make_uint2(pack_bf2(y.x, y.y), pack_bf2(y.z, y.w));
-        }
+        if (is_k && i + RS < iters) tload(i + RS, tb[u]);
       }
     }
   }
@@ -300,7 +356,8 @@ extern "C" mkx_status mkx_prep_run(mkx_prep_handle* h, const uint16_t* src, int 
   if (!h || !src || !cos || !sin || !k_out || !v_out) return MKX_ERR_INVALID_ARG;
   if (S < 1 || S > 4096 || SP < S) return MKX_ERR_INVALID_ARG;
   if ((reinterpret_cast<uintptr_t>(src) & 15) != 0 || (reinterpret_cast<uintptr_t>(k_out) & 15) != 0 ||
-      (reinterpret_cast<uintptr_t>(v_out) & 15) != 0)
+      (reinterpret_cast<uintptr_t>(v_out) & 15) != 0 || (reinterpret_cast<uintptr_t>(cos) & 15) != 0 ||
+      (reinterpret_cast<uintptr_t>(sin) & 15) != 0)
     return MKX_ERR_INVALID_ARG;
   mkx::DeviceScope dev_scope(h->device);
   if (dev_scope.err != cudaSuccess) return MKX_ERR_CUDA;

@@ -65,6 +65,27 @@ def test_padding_rows_untouched():
     rp.close()
 
 
+def test_unaligned_rope_tables_rejected():
+    """The epilogue reads the RoPE tables as 16-byte vectors: a table that does not start on a 16-byte
+    boundary is refused before the launch."""
+    from reki_megakernel_b200 import _lib
+    from reki_megakernel_b200.prepare import RegisterPrepare
+    d = ExpertDims(L=1)
+    rp = RegisterPrepare(make_prepare_weights(d, seed=0).to(DEV))
+    src = make_source(8, d.src_dim, seed=0).to(DEV)
+    c, s = (t.to(DEV) for t in rope_cos_sin(torch.arange(9), d.HD))
+    cu = c.reshape(-1)[1:1 + 8 * d.HD].view(8, d.HD)  # 4 bytes past a 16-byte boundary
+    su = s.reshape(-1)[1:1 + 8 * d.HD].view(8, d.HD)
+    with pytest.raises(_lib.MkxError):
+        rp.run(src, cu, su)
+    with pytest.raises(_lib.MkxError):
+        rp.run(src, c[:8], su)
+    rp.run(src, c[:8], s[:8])  # aligned: accepted
+    torch.cuda.synchronize()
+    rp.check_device_error()
+    rp.close()
+
+
 def test_prepare_graph_capture_and_feeds_the_expert():
     """Captured in a CUDA graph; its K/V are the layout ExpertMegakernel reads."""
     from reki_megakernel_b200.prepare import RegisterPrepare
