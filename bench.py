@@ -417,7 +417,7 @@ def run_full(args):
     fp.check_device_errors()
     L, H, I = dims.L, dims.H, dims.I
     layer_w = L * (3 * H * H + 3 * H * H + 3 * I * H) * 2
-    reg_launches = bx.launches(R // 16, 16, 1) - 2 + L  # the pass: per layer the loop's launches plus the frame write
+    reg_launches = bx.launches(R // 16, 16, 1) - 2  # the pass: per layer the loop's launches (no tails)
     wbytes = (N * algorithmic_bytes_per_step(dims, dims.MODW * 2) + layer_w + dims.MODW * H * 2 + dims.MODW * 4
               + L * 2 * H * dims.src_dim * 2)
     ms = statistics.mean(per)

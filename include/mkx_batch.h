@@ -89,7 +89,7 @@ typedef struct {
   int R;                    /* register rows: a multiple of 16, <= 16 * max_episodes */
 } mkx_register_inputs;
 
-/* Enqueues the register pass on `stream` (12 launches per layer, programmatic dependents, no
+/* Enqueues the register pass on `stream` (11 launches per layer, programmatic dependents, no
  * host synchronisation, capturable). Uses the handle's activation buffers: not concurrent with
  * mkx_batch_run on the same handle. */
 mkx_status mkx_batch_register_pass(mkx_batch_handle* h, const mkx_register_inputs* in, cudaStream_t stream);

@@ -442,6 +442,13 @@ struct AttnParams {
   int kv_input;          // 1: K / V and lim were in memory before the launch sequence (staged early)
   int ca_all;            // CA: 1 = the whole padded source (kcap rows) staged at once
   int lim_stride;        // episode stride of lim (0: one value for all episodes)
+  // SA, register pass: the memory rows [frame_row0, kv_rows) are this layer's frame, the K (per-head
+  // norm + RoPE) and V of the frame_rows rows of src, computed here: placed after the older rows in
+  // shared memory, and written to the memory (mk_out / mv_out, episode e writes its own T rows).
+  // frame_row0 < 0: none.
+  int frame_row0, frame_rows;
+  uint16_t* mk_out;
+  uint16_t* mv_out;
   float qk_eps, scale;
 };
 
@@ -480,12 +487,13 @@ __global__ void __launch_bounds__(32 * ATT_WARPS) bt_attention(const __grid_cons
       reinterpret_cast<uint32_t*>(Vs + (size_t)j * KS)[q] = zero;
     }
   };
-  int nm = 0, nk = 0, S = 0;
+  int nm = 0, nk = 0, S = 0, k0 = 0;
+  const bool frame = SA && p.frame_row0 >= 0;
   if (SA) {
-    const int k0 = min(max(p.lim[e * p.lim_stride], 0), p.kv_rows);
+    k0 = min(max(p.lim[e * p.lim_stride], 0), p.kv_rows);
     nm = p.kv_rows - k0;
     nk = nm + (p.own ? T : 0);
-    stage(k0, nm, 0, tid, 32 * ATT_WARPS);
+    stage(k0, frame ? max(p.frame_row0 - k0, 0) : nm, 0, tid, 32 * ATT_WARPS);  // rows written before the sequence
     zero_rows(nk, (nk + CA_BLK - 1) / CA_BLK * CA_BLK, tid, 32 * ATT_WARPS);
   } else {
     S = min(max(p.lim[e * p.lim_stride], 1), p.kv_rows);
@@ -496,28 +504,80 @@ __global__ void __launch_bounds__(32 * ATT_WARPS) bt_attention(const __grid_cons
   cp_async_commit();
   if (p.kv_input) grid_dep_wait();  // the queries are the previous kernel's output
   if (tid == 0) grid_dep_launch();
-  // queries (and SA own keys / values), bf16, rows >= T zero: warp w takes rows w, w + 4, ...
-  for (int t = warp; t < 16; t += ATT_WARPS) {
-    uint32_t qv = 0u;
-    if (t < T) {
-      const size_t m = (size_t)e * T + t;
-      const float2 cs = *reinterpret_cast<const float2*>(p.cos + m * HD + 2 * lane);
-      const float2 sn = *reinterpret_cast<const float2*>(p.sin + m * HD + 2 * lane);
-      const uint16_t* row = p.src + m * p.src_ld + h * HD;
-      uint32_t u = *reinterpret_cast<const uint32_t*>(row + 2 * lane);
-      const float2 q = norm_rope_row(bf_lo(u), bf_hi(u), *reinterpret_cast<const float2*>(p.wq + 2 * lane), cs, sn,
-                                     p.qk_eps, lane);
-      qv = pack_bf2(q.x, q.y);
-      if (SA && p.own) {
-        u = *reinterpret_cast<const uint32_t*>(row + H + 2 * lane);
-        const float2 k = norm_rope_row(bf_lo(u), bf_hi(u), *reinterpret_cast<const float2*>(p.wk + 2 * lane), cs, sn,
-                                       p.qk_eps, lane);
-        reinterpret_cast<uint32_t*>(Ks + (size_t)(nm + t) * KS)[lane] = pack_bf2(k.x, k.y);
-        reinterpret_cast<uint32_t*>(Vs + (size_t)(nm + t) * KS)[lane] =
-            *reinterpret_cast<const uint32_t*>(row + 2 * H + 2 * lane);
+  // queries (and SA own keys / values), bf16, rows >= T zero: warp w takes rows w, w + 4, ...; every
+  // global load of the warp's rows goes out before the first row's arithmetic (one L2 round trip)
+  constexpr int QR = 16 / ATT_WARPS;
+  {
+    uint32_t qu[QR], ku[QR], vu[QR];
+    float2 cs[QR], sn[QR];
+#pragma unroll
+    for (int j = 0; j < QR; ++j) {
+      const int t = warp + ATT_WARPS * j;
+      if (t < T) {
+        const size_t m = (size_t)e * T + t;
+        cs[j] = *reinterpret_cast<const float2*>(p.cos + m * HD + 2 * lane);
+        sn[j] = *reinterpret_cast<const float2*>(p.sin + m * HD + 2 * lane);
+        const uint16_t* row = p.src + m * p.src_ld + h * HD;
+        qu[j] = *reinterpret_cast<const uint32_t*>(row + 2 * lane);
+        if (SA && p.own) {
+          ku[j] = *reinterpret_cast<const uint32_t*>(row + H + 2 * lane);
+          vu[j] = *reinterpret_cast<const uint32_t*>(row + 2 * H + 2 * lane);
+        }
       }
     }
-    reinterpret_cast<uint32_t*>(Qs + (size_t)t * KS)[lane] = qv;
+    const float2 wq = *reinterpret_cast<const float2*>(p.wq + 2 * lane);
+#pragma unroll
+    for (int j = 0; j < QR; ++j) {
+      const int t = warp + ATT_WARPS * j;
+      uint32_t qv = 0u;
+      if (t < T) {  // warp-uniform: the norm's shuffles need all lanes
+        const float2 q = norm_rope_row(bf_lo(qu[j]), bf_hi(qu[j]), wq, cs[j], sn[j], p.qk_eps, lane);
+        qv = pack_bf2(q.x, q.y);
+        if (SA && p.own) {
+          const float2 k = norm_rope_row(bf_lo(ku[j]), bf_hi(ku[j]), *reinterpret_cast<const float2*>(p.wk + 2 * lane),
+                                         cs[j], sn[j], p.qk_eps, lane);
+          reinterpret_cast<uint32_t*>(Ks + (size_t)(nm + t) * KS)[lane] = pack_bf2(k.x, k.y);
+          reinterpret_cast<uint32_t*>(Vs + (size_t)(nm + t) * KS)[lane] = vu[j];
+        }
+      }
+      reinterpret_cast<uint32_t*>(Qs + (size_t)t * KS)[lane] = qv;
+    }
+  }
+  if (frame) {  // the frame's K / V from the QKV output (same rounding as the action rows' own keys)
+    constexpr int FU = 8;  // rows per warp and round, loaded before any is processed
+    const float2 wk = *reinterpret_cast<const float2*>(p.wk + 2 * lane);
+    for (int m0 = warp; m0 < p.frame_rows; m0 += ATT_WARPS * FU) {
+      uint32_t ku[FU], vu[FU];
+      float2 cs[FU], sn[FU];
+#pragma unroll
+      for (int j = 0; j < FU; ++j) {
+        const int m = m0 + ATT_WARPS * j;
+        if (m < p.frame_rows) {
+          const uint16_t* row = p.src + (size_t)m * p.src_ld + h * HD;
+          ku[j] = *reinterpret_cast<const uint32_t*>(row + H + 2 * lane);
+          vu[j] = *reinterpret_cast<const uint32_t*>(row + 2 * H + 2 * lane);
+          cs[j] = *reinterpret_cast<const float2*>(p.cos + (size_t)m * HD + 2 * lane);
+          sn[j] = *reinterpret_cast<const float2*>(p.sin + (size_t)m * HD + 2 * lane);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < FU; ++j) {
+        const int m = m0 + ATT_WARPS * j;
+        if (m < p.frame_rows) {  // warp-uniform
+          const float2 k = norm_rope_row(bf_lo(ku[j]), bf_hi(ku[j]), wk, cs[j], sn[j], p.qk_eps, lane);
+          const uint32_t kv = pack_bf2(k.x, k.y);
+          const int r = p.frame_row0 + m;
+          if (r >= k0) {
+            reinterpret_cast<uint32_t*>(Ks + (size_t)(r - k0) * KS)[lane] = kv;
+            reinterpret_cast<uint32_t*>(Vs + (size_t)(r - k0) * KS)[lane] = vu[j];
+          }
+          if (m / T == e) {
+            *reinterpret_cast<uint32_t*>(p.mk_out + (size_t)r * H + h * HD + 2 * lane) = kv;
+            *reinterpret_cast<uint32_t*>(p.mv_out + (size_t)r * H + h * HD + 2 * lane) = vu[j];
+          }
+        }
+      }
+    }
   }
   // Every warp takes the 16-key slice [64 b + 16 warp, + 16) of each 64-key block b, with its own
   // softmax statistics (rows g and g + 8 of the quad's lanes); the warps' partial results are merged
@@ -685,28 +745,6 @@ __global__ void __launch_bounds__(32 * ATT_WARPS) bt_attention(const __grid_cons
   }
 }
 
-// The register pass's own K (per-head RMSNorm with 1 + k_norm, then RoPE at the rows' positions, a bf16
-// rounding after each, as every key the self-attention reads) and V of one layer, written into the
-// memory rows [row0, row0 + R) of that layer before its self-attention reads the memory: one warp per
-// (row, head).
-__global__ void __launch_bounds__(256) bt_write_frame(const uint16_t* __restrict__ qkv, int R, uint16_t* mk, uint16_t* mv,
-                                                      int row0, const float* __restrict__ wk, const float* __restrict__ cos,
-                                                      const float* __restrict__ sin, float eps) {
-  grid_dep_wait();
-  if (threadIdx.x == 0) grid_dep_launch();
-  const int w = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-  if (w >= R * NH) return;  // whole warps
-  const int r = w / NH, hh = w % NH;
-  const uint16_t* row = qkv + (size_t)r * 3 * H + hh * HD + 2 * lane;
-  const uint32_t u = *reinterpret_cast<const uint32_t*>(row + H);
-  const float2 k = norm_rope_row(bf_lo(u), bf_hi(u), *reinterpret_cast<const float2*>(wk + 2 * lane),
-                                 *reinterpret_cast<const float2*>(cos + (size_t)r * HD + 2 * lane),
-                                 *reinterpret_cast<const float2*>(sin + (size_t)r * HD + 2 * lane), eps, lane);
-  *reinterpret_cast<uint32_t*>(mk + (size_t)(row0 + r) * H + hh * HD + 2 * lane) = pack_bf2(k.x, k.y);
-  *reinterpret_cast<uint32_t*>(mv + (size_t)(row0 + r) * H + hh * HD + 2 * lane) =
-      *reinterpret_cast<const uint32_t*>(row + 2 * H);
-}
-
 // ---------------------------------------------------------------------------------------------
 // Step tail (src/mk_expert.py:254-299), one CTA of 256 threads per action row (episode e, row t):
 // o = bf16(AdaRMS_final(h)), v_a = o . Wout[a] + bout[a] (fp32, a < A), x_a <- (a < action_dim ? x_a
@@ -729,13 +767,23 @@ struct TailParams {
 };
 
 __global__ void __launch_bounds__(256) bt_tail(const __grid_constant__ TailParams p) {
-  grid_dep_wait();
-  if (threadIdx.x == 0) grid_dep_launch();
   __shared__ float red[8][32];
   __shared__ float xnew[32];
   __shared__ float ssum[8];
   const int e = blockIdx.x / p.T, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const size_t m = blockIdx.x;  // = e * T + t
+  // the final norm's modulation columns are inputs of the launch sequence: read before the wait
+  float ms[3], mh[3];
+  if (!p.first) {
+    const uint16_t* mf = p.mfin + (size_t)e * p.ep_stride;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      ms[k] = bf_at(mf[tid + 256 * k]);
+      mh[k] = bf_at(mf[H + tid + 256 * k]);
+    }
+  }
+  grid_dep_wait();
+  if (threadIdx.x == 0) grid_dep_launch();
   float* xr = p.xs + m * p.A;
   if (p.first) {
     if (tid < p.A) {
@@ -758,21 +806,28 @@ __global__ void __launch_bounds__(256) bt_tail(const __grid_constant__ TailParam
 #pragma unroll
     for (int w = 0; w < 8; ++w) tot += ssum[w];
     const float rstd = rsqrtf(tot / (float)H + p.eps);
-    const uint16_t* mf = p.mfin + (size_t)e * p.ep_stride;
     float o[3];
 #pragma unroll
-    for (int k = 0; k < 3; ++k) {
-      const int col = tid + 256 * k;
-      o[k] = round_bf(fmaf(hv[k] * rstd, 1.f + bf_at(mf[col]), bf_at(mf[H + col])));
-    }
-    // v_a for every a < A: per-thread partials over its 3 columns, then warp and block sums
-    for (int a = 0; a < p.A; ++a) {
-      float v = o[0] * p.wout[a * H + tid];
-      v = fmaf(o[1], p.wout[a * H + tid + 256], v);
-      v = fmaf(o[2], p.wout[a * H + tid + 512], v);
+    for (int k = 0; k < 3; ++k) o[k] = round_bf(fmaf(hv[k] * rstd, 1.f + ms[k], mh[k]));
+    // v_a for every a < A: per-thread partials over its 3 columns, then warp and block sums; the
+    // weights of 8 outputs are loaded before any of them is summed (one L2 round trip per 8)
+    for (int a0 = 0; a0 < p.A; a0 += 8) {
+      float w[8][3];
 #pragma unroll
-      for (int s = 16; s >= 1; s >>= 1) v += __shfl_xor_sync(0xffffffffu, v, s);
-      if (lane == 0) red[warp][a] = v;
+      for (int j = 0; j < 8; ++j)
+        if (a0 + j < p.A)
+#pragma unroll
+          for (int k = 0; k < 3; ++k) w[j][k] = p.wout[(a0 + j) * H + tid + 256 * k];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (a0 + j >= p.A) break;  // block-uniform
+        float v = o[0] * w[j][0];
+        v = fmaf(o[1], w[j][1], v);
+        v = fmaf(o[2], w[j][2], v);
+#pragma unroll
+        for (int s = 16; s >= 1; s >>= 1) v += __shfl_xor_sync(0xffffffffu, v, s);
+        if (lane == 0) red[warp][a0 + j] = v;
+      }
     }
     __syncthreads();
     if (tid < p.A) {
@@ -1137,8 +1192,8 @@ void seq_adarms(Seq& q, const uint16_t* blk) {
 // What one layer reads besides the handle's buffers: the episodes' register memory and
 // cross-attention K/V of this layer (episode strides kvm_ep / kvc_ep; 0 = shared by all), their row
 // limits (lim_stride 0 = one value for all), the RoPE tables of the query rows, and -- register pass
-// only -- the memory rows [frame_row0, frame_row0 + M) where the rows' own K / V go before the
-// self-attention reads the memory (own = 0: no own-row keys besides).
+// only -- the memory rows [frame_row0, frame_row0 + M) where the self-attention launch writes the
+// rows' own K / V (and reads them as the memory's newest rows; own = 0: no own-row keys besides).
 struct LayerIO {
   const uint16_t* memk;
   const uint16_t* memv;
@@ -1156,7 +1211,7 @@ struct LayerIO {
   int frame_row0;  // < 0: no frame to write
 };
 
-// The 11-12 launches of one layer (src/mk_expert.py:342-421); blk: this layer's modulation blocks
+// The 11 launches of one layer (src/mk_expert.py:342-421); blk: this layer's modulation blocks
 // [SA | CA | MLP] x [scale, shift, gate] of episode 0.
 void seq_layer(Seq& q, int l, const uint16_t* blk, const LayerIO& io) {
   mkx_batch_handle* h = q.h;
@@ -1181,10 +1236,6 @@ void seq_layer(Seq& q, int l, const uint16_t* blk, const LayerIO& io) {
   // self-attention block
   seq_adarms(q, blk);
   seq_gemm(q, G_QKV, l, 0, h->qkv, 3 * H, nullptr);
-  if (io.frame_row0 >= 0 && q.err == cudaSuccess && q.st == MKX_OK)
-    q.err = launch_pdl(bt_write_frame, dim3((q.M * NH + 7) / 8), dim3(256), 0, q.stream, (const uint16_t*)h->qkv, q.M,
-                       const_cast<uint16_t*>(memk_l), const_cast<uint16_t*>(memv_l), io.frame_row0,
-                       (const float*)(h->nrm + (size_t)(L + l) * HD), io.sa_cos, io.sa_sin, h->d.qk_eps);
   ap.src = h->qkv;
   ap.src_ld = 3 * H;
   ap.kb = memk_l;
@@ -1199,8 +1250,16 @@ void seq_layer(Seq& q, int l, const uint16_t* blk, const LayerIO& io) {
   ap.kcap = kcap;
   ap.own = io.own;
   ap.kv_input = io.sa_input;
+  ap.frame_row0 = -1;
+  if (io.frame_row0 >= 0) {
+    ap.frame_row0 = io.frame_row0;
+    ap.frame_rows = q.M;
+    ap.mk_out = const_cast<uint16_t*>(memk_l);
+    ap.mv_out = const_cast<uint16_t*>(memv_l);
+  }
   if (q.err == cudaSuccess && q.st == MKX_OK)
     q.err = launch_pdl(bt_attention<true>, dim3(q.B * NH), dim3(32 * ATT_WARPS), att_sa, q.stream, ap);
+  ap.frame_row0 = -1;
   seq_gemm(q, G_O, l, 1, h->h, H, blk + 2 * H);
   // cross-attention block
   seq_adarms(q, blk + 3 * H);
@@ -1348,7 +1407,7 @@ extern "C" mkx_status mkx_batch_register_pass(mkx_batch_handle* h, const mkx_reg
   io.src_rows = in->src_rows;
   io.lim_stride = 0;
   io.own = 0;
-  io.sa_input = 0;  // the frame's rows are written by the pass itself
+  io.sa_input = 1;  // the memory rows below the frame; the frame's come from the QKV output (frame_row0)
   io.ca_input = 1;
   io.sa_cos = in->sa_cos;
   io.sa_sin = in->sa_sin;
