@@ -118,6 +118,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) bt_gemm(const __grid_constant
   uint16_t* res_s = reinterpret_cast<uint16_t*>(reinterpret_cast<char*>(bars) + 256);
   const bool pre_res = p.epi == E_GATED;
 
+  int issued = 0;  // producer (thread 0)
+  const uint16_t* wsrc = p.wpk + (size_t)tile * p.ktiles * (A_BYTES / 2);
+  const int pre = nk < STAGES ? nk : STAGES;
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
@@ -126,23 +129,23 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1) bt_gemm(const __grid_constant
     mbar_init(done, 1);
     *consumed_slot = 0;
     fence_mbar_init();
+    // the W tiles of the first stages need nothing from the previous kernel: they go out before the
+    // TMEM allocation and the block barrier
+    const uint64_t pol = l2_evict_first();
+    for (int i = 0; i < pre; ++i) {
+      mbar_expect_tx(&full[i], (uint32_t)stage_bytes);
+      bulk_g2s_hint(ring + i * stage_bytes, wsrc + (size_t)(kt0 + i) * (A_BYTES / 2), (uint32_t)A_BYTES, &full[i], pol);
+    }
   }
   if (warp == 1) tmem_alloc(tmem_slot, (uint32_t)p.tmem_cols);
   __syncthreads();
   tmem_fence_after();
   const uint32_t tmem = *tmem_slot;
-  int issued = 0;
   if (threadIdx.x == 0) grid_dep_launch();  // the next kernel's CTAs may take free SMs and start their W
 
   if (warp == 0 && lane == 0) {
-    // producer: the W tiles of the first stages need nothing from the previous kernel
-    const uint16_t* wsrc = p.wpk + (size_t)tile * p.ktiles * (A_BYTES / 2);
+    // producer
     const uint64_t pol = l2_evict_first();
-    const int pre = nk < STAGES ? nk : STAGES;
-    for (int i = 0; i < pre; ++i) {
-      mbar_expect_tx(&full[i], (uint32_t)stage_bytes);
-      bulk_g2s_hint(ring + i * stage_bytes, wsrc + (size_t)(kt0 + i) * (A_BYTES / 2), (uint32_t)A_BYTES, &full[i], pol);
-    }
     grid_dep_wait();  // the token rows are the previous kernel's output
     for (int i = 0; i < nk; ++i) {
       const int s = i % STAGES, kb = kt0 + i;
