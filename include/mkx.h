@@ -194,6 +194,15 @@ mkx_status mkx_run_static(const mkx_dims* dims, const mkx_packed_weights* w, con
  * one call each instead of one host call per tensor. No counterpart in the reference. */
 mkx_status mkx_h2d_copies(int n, void* const* dst, const void* const* src, const size_t* bytes, cudaStream_t stream);
 
+/* Enqueues n pitched host-to-device copies on `stream`, one cudaMemcpy2DAsync each, in order: height[i]
+ * rows of width[i] bytes from src[i] (pinned host, rows spitch[i] bytes apart) to dst[i] (device, rows
+ * dpitch[i] bytes apart); width[i] <= both pitches, height[i] >= 1 (MKX_ERR_INVALID_ARG otherwise,
+ * before anything is enqueued). Streamed launches use it to copy only the K/V rows the kernel reads
+ * (memory rows from kv_start, source rows below S) of a run of layers with one command. No
+ * counterpart in the reference. */
+mkx_status mkx_h2d_copies_2d(int n, void* const* dst, const size_t* dpitch, const void* const* src,
+                             const size_t* spitch, const size_t* width, const size_t* height, cudaStream_t stream);
+
 /* Last CUDA error string seen by the library (thread-local, static storage). */
 const char* mkx_last_cuda_error(void);
 

@@ -81,6 +81,7 @@ SIGNATURES = {
     "mkx_run_static": (C.c_int, [C.POINTER(Dims), C.POINTER(PackedWeights), C.POINTER(StepInputs), P, P]),
     "mkx_last_cuda_error": (C.c_char_p, []),
     "mkx_h2d_copies": (C.c_int, [C.c_int, P, P, P, P]),
+    "mkx_h2d_copies_2d": (C.c_int, [C.c_int, P, P, P, P, P, P, P]),
     "mkx_destroy": (None, [P]),
     "mkx_batch_create": (C.c_int, [C.POINTER(Dims), C.POINTER(Weights), C.c_int, C.c_int, C.POINTER(P)]),
     "mkx_batch_run": (C.c_int, [P, C.POINTER(BatchInputs), P]),

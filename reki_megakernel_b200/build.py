@@ -21,7 +21,7 @@ LIB = PKG / "libmkx.so"
 # %globaltimer at numbered points inside each stage); loaded only after _lib.use_traced_build().
 TRACE_LIB = PKG / "libmkx_trace.so"
 SOURCES = [PKG / "csrc" / "mk_expert.cu", PKG / "csrc" / "mk_prepare.cu", PKG / "csrc" / "mk_mods.cu",
-           PKG / "csrc" / "mk_batch.cu"]
+           PKG / "csrc" / "mk_batch.cu", PKG / "csrc" / "mk_copies.cu"]
 HEADERS = [PKG / "csrc" / "mkx_device.cuh", PKG / "csrc" / "mkx_tma.cuh", ROOT / "include" / "mkx.h",
            ROOT / "include" / "mkx_prepare.h", ROOT / "include" / "mkx_mods.h", ROOT / "include" / "mkx_batch.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

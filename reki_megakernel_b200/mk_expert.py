@@ -68,26 +68,26 @@ def _copy_groups(L: int):
     return out
 
 
-def _merged(pairs):
-    """(dst, src) copies of consecutive layers, merged where both the device and the host tensors
-    continue each other in memory (one copy instead of several)."""
+def _rows2d(dev_layers, host_layers, r0: int, r1: int):
+    """Pitched copies (dst, dpitch, src, spitch, width, height) of rows [r0, r1) of consecutive layers
+    (each a contiguous [rows, ...] tensor, the range clipped to its rows): one copy for each run of
+    layers whose device and host tensors both follow each other at one pitch."""
     out = []
-    for d, h in pairs:
+    for d, h in zip(dev_layers, host_layers):
+        rows = d.shape[0]
+        a, z = min(max(r0, 0), rows), min(max(r1, 0), rows)
+        if z <= a:
+            continue
+        rb = (d.numel() // rows) * d.element_size()  # bytes per row
+        dp, hp, w = d.data_ptr() + a * rb, h.data_ptr() + a * rb, (z - a) * rb
+        pitch = rows * rb
         if out:
-            pd, ph = out[-1]
-            if (pd.data_ptr() + pd.numel() * pd.element_size() == d.data_ptr()
-                    and ph.data_ptr() + ph.numel() * ph.element_size() == h.data_ptr()
-                    and pd.dtype == d.dtype and ph.dtype == h.dtype):
-                n = pd.numel() + d.numel()
-                out[-1] = (_flat(pd, n), _flat(ph, n))
+            pd, pdp, ph, php, pw, n = out[-1]
+            if pw == w and pdp == pitch and php == pitch and pd + n * pitch == dp and ph + n * pitch == hp:
+                out[-1] = (pd, pdp, ph, php, pw, n + 1)
                 continue
-        out.append((d, h))
+        out.append((dp, pitch, hp, pitch, w, 1))
     return out
-
-
-def _flat(t: torch.Tensor, n: int) -> torch.Tensor:
-    """A 1-D view of n elements starting at t's first element (t contiguous)."""
-    return torch.as_strided(t, (n,), (1,))
 
 
 class ExpertMegakernel:
@@ -252,9 +252,11 @@ class ExpertMegakernel:
 
         On the current stream the small inputs (x_t, mods, dt, RoPE tables, cu_kv, cu_src) are copied
         in; on a side stream that first waits for this handle's previous launch (it read the same
-        buffers), per layer the memory and cross-attention K/V and a 4-byte readiness word, all plain
-        host-to-device copies issued by the library (a kernel on that stream would wait for the SMs
-        the launch holds); then the launch is enqueued on the current stream. The launch waits for
+        buffers), per group of layers the memory and cross-attention K/V rows the launch reads
+        (memory rows from cu_kv[0], source rows below cu_src[1]: one pitched copy per kind and group)
+        and a 4-byte readiness word, all plain host-to-device copies issued by the library (a kernel
+        on that stream would wait for the SMs the launch holds); then the launch is enqueued on the
+        current stream. ``last_h2d_bytes`` is the number of bytes the call copied in. The launch waits for
         layer l's word before reading its K/V, so the K/V copies run under the first Euler step
         instead of ahead of the launch. Successive calls may come from different current streams:
         each call's copies wait for the previous call's launch. The host tensors must stay alive
@@ -307,18 +309,25 @@ class ExpertMegakernel:
         main = torch.cuda.current_stream(dev)
         if b["prev"] is not None and b["prev_stream"] != main:
             main.wait_event(b["prev"])  # the previous launch, on another stream, still reads b["in"]
+        # the kernel reads memory rows [kv_start, PM) and source rows [0, S) only: the others stay
+        # on the host (their device rows keep whatever they held, which no launch reads)
+        rows = (int(host["cu_kv"][0]), int(host["cu_src"][1]))
         plan = b.get("plan")
-        if plan is None or plan["seen"] != seen:
-            # the copy lists for these host tensors, as library-call arguments built once; the readiness
-            # words' sources (the ring row of the call) are patched in per call
+        if plan is None or plan["seen"] != seen or plan["rows"] != rows:
+            # the copy lists for these host tensors and row ranges, as library-call arguments built
+            # once; the readiness words' sources (the ring row of the call) are patched in per call
             side, ready_at = [], []
             for l0, l1 in _copy_groups(self.L):
                 for j in range(4):  # memory K, V, cross-attention K, V of layers l0..l1-1
-                    side += _merged([(b["kv"][l][j], kv[l][j]) for l in range(l0, l1)])
+                    r0, r1 = (rows[0], 1 << 30) if j < 2 else (0, rows[1])
+                    side += _rows2d([b["kv"][l][j] for l in range(l0, l1)], [kv[l][j] for l in range(l0, l1)], r0, r1)
                 ready_at.append((len(side), l0, l1))
-                side.append((b["ready"][l0:l1], b["ring"][0][l0:l1]))
-            plan = {"seen": seen, "small": self._h2d_args([(b["in"][k], v) for k, v in host.items()]),
-                    "side": self._h2d_args(side), "ready_at": ready_at}
+                w = 4 * (l1 - l0)
+                side.append((b["ready"][l0:l1].data_ptr(), w, b["ring"][0][l0:l1].data_ptr(), w, w, 1))
+            small = [(b["in"][k], v) for k, v in host.items()]
+            plan = {"seen": seen, "rows": rows, "small": self._h2d_args(small), "side": self._h2d2_args(side),
+                    "ready_at": ready_at,
+                    "bytes": sum(v.numel() * v.element_size() for _, v in small) + sum(e[4] * e[5] for e in side)}
             b["plan"] = plan
         self._h2d_run(plan["small"], main)
         b["seq"] += 1
@@ -333,8 +342,9 @@ class ExpertMegakernel:
             cs.wait_event(b["prev"])  # the previous launch has finished with the buffers
         side = plan["side"]
         for idx, l0, l1 in plan["ready_at"]:  # this call's ring row
-            side[2][idx] = row[l0:l1].data_ptr()
-        self._h2d_run(side, cs)  # enqueued before the launch: the copies start while it is prepared
+            side[3][idx] = row[l0:l1].data_ptr()
+        self._h2d2_run(side, cs)  # enqueued before the launch: the copies start while it is prepared
+        self.last_h2d_bytes = plan["bytes"]
         ev = torch.cuda.Event()
         ev.record(cs)
         if b.get("si") is None or b["dt_key"] != (None if "dt" in host else float(dt)):
@@ -393,6 +403,20 @@ class ExpertMegakernel:
         src = (C.c_void_p * n)(*[ss.data_ptr() for _, ss in pairs])
         nb = (C.c_size_t * n)(*[ss.numel() * ss.element_size() for _, ss in pairs])
         return [n, dst, src, nb]
+
+    @staticmethod
+    def _h2d2_args(entries):
+        """[n, dst, dpitch, src, spitch, width, height] library-call arguments of pitched copies."""
+        n = len(entries)
+        cols = list(zip(*entries)) if entries else [()] * 6
+        kinds = (C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t)
+        return [n] + [(k * n)(*c) for k, c in zip(kinds, cols)]
+
+    def _h2d2_run(self, args, stream) -> None:
+        """The pitched copies of `args` (from _h2d2_args) in order on `stream`, one library call."""
+        n, dst, dp, src, sp, w, h = args
+        _lib.check(self._lib.mkx_h2d_copies_2d(n, dst, dp, src, sp, w, h, C.c_void_p(stream.cuda_stream)),
+                   "mkx_h2d_copies_2d")
 
     def _h2d_run(self, args, stream) -> None:
         """The copies of `args` (from _h2d_args) in order on `stream`, one library call for all."""

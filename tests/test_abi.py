@@ -156,6 +156,16 @@ def test_host_copy_arguments_are_checked_without_a_device():
     assert lib.mkx_h2d_copies(-1, None, None, None, None) == _lib.MKX_ERR_INVALID_ARG
     assert lib.mkx_h2d_copies(2, None, None, None, None) == _lib.MKX_ERR_INVALID_ARG
     assert lib.mkx_h2d_copies(0, None, None, None, None) == _lib.MKX_OK   # nothing to copy
+    assert lib.mkx_h2d_copies_2d(-1, None, None, None, None, None, None, None) == _lib.MKX_ERR_INVALID_ARG
+    assert lib.mkx_h2d_copies_2d(1, None, None, None, None, None, None, None) == _lib.MKX_ERR_INVALID_ARG
+    assert lib.mkx_h2d_copies_2d(0, None, None, None, None, None, None, None) == _lib.MKX_OK
+    one = lambda t, v: (t * 1)(v)  # noqa: E731
+    bad = [  # (dst, dpitch, src, spitch, width, height): a null pointer, width past a pitch, no rows
+        (0, 64, 0x1000, 64, 64, 1), (0x1000, 32, 0x2000, 64, 64, 1), (0x1000, 64, 0x2000, 32, 64, 1),
+        (0x1000, 64, 0x2000, 64, 64, 0)]
+    for d, dp, s_, sp, w, h in bad:  # rejected before any copy is enqueued
+        assert lib.mkx_h2d_copies_2d(1, one(C.c_void_p, d), one(C.c_size_t, dp), one(C.c_void_p, s_), one(C.c_size_t, sp),
+                                     one(C.c_size_t, w), one(C.c_size_t, h), None) == _lib.MKX_ERR_INVALID_ARG
 
 
 def test_readiness_values_never_repeat_consecutively():

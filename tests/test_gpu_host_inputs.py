@@ -96,3 +96,46 @@ def test_run_from_host_on_alternating_streams(full):
     mk.check_device_error()
     for got, want in zip(gots, wants):
         assert torch.equal(got, want)
+
+
+def test_run_from_host_copies_only_the_rows_read(full):
+    """One set of pinned host buffers refilled in place between calls (a control loop), with
+    kv_start and S changing from call to call and NaN in every row the kernel must not read: each
+    result equals ``run`` on the same inputs on the device, and the call copies exactly the memory
+    rows [kv_start, PM) and the source rows [0, S) of every layer besides the small inputs."""
+    dims, mk = full
+    cases = [make_inputs(dims, S=S, SP=192, frames_valid=fv, seed=30 + i, noise_seed=300 + i, poison=True)
+             for i, (S, fv) in enumerate([(160, 1), (64, 3), (100, 2), (160, 3)])]
+    wants = []
+    for inp in cases:
+        d = inp.to(DEV)
+        wants.append(mk.run(d.x[:1], d.mods[0], d.dt[:1], make_past(d), d.action_dim).clone())
+    torch.cuda.synchronize()
+    pin = lambda t: t.contiguous().pin_memory()  # noqa: E731
+    x, mods, dt = pin(cases[0].x[:1]), pin(cases[0].mods[0]), pin(cases[0].dt[:1])
+    hp = _pinned_past(cases[0])
+    row_bytes = dims.NH * dims.HD * 2
+    for inp, want in zip(cases, wants):
+        src = make_past(inp)
+        x.copy_(inp.x[:1])
+        mods.copy_(inp.mods[0])
+        dt.copy_(inp.dt[:1])
+        for (hk, hv), (k, v) in zip(hp.register_step["mem_kv"], src.register_step["mem_kv"]):
+            hk.copy_(k)
+            hv.copy_(v)
+        for (hk, hv), (k, v) in zip(hp.cross_attn_kv, src.cross_attn_kv):
+            hk.copy_(k)
+            hv.copy_(v)
+        for key in ("cu_kv", "cu_src"):
+            hp.register_step[key].copy_(src.register_step[key])
+        for key in ("sa_pe", "ca_pe"):
+            for t, s in zip(hp.register_step[key], src.register_step[key]):
+                t.copy_(s)
+        got = mk.run_from_host(x, mods, dt, hp, inp.action_dim)
+        torch.cuda.synchronize()
+        mk.check_device_error()
+        assert torch.equal(got, want)
+        st = hp.register_step
+        small = sum(t.numel() * t.element_size() for t in (x, mods, dt, st["cu_kv"], st["cu_src"], *st["sa_pe"], *st["ca_pe"]))
+        PM, kv0, S = st["mem_kv"][0][0].shape[0], int(st["cu_kv"][0]), int(st["cu_src"][1])
+        assert mk.last_h2d_bytes == small + dims.L * 2 * row_bytes * ((PM - kv0) + S) + 4 * dims.L
