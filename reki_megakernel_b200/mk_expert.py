@@ -310,8 +310,14 @@ class ExpertMegakernel:
         if b["prev"] is not None and b["prev_stream"] != main:
             main.wait_event(b["prev"])  # the previous launch, on another stream, still reads b["in"]
         # the kernel reads memory rows [kv_start, PM) and source rows [0, S) only: the others stay
-        # on the host (their device rows keep whatever they held, which no launch reads)
+        # on the host (their device rows keep whatever they held, which no launch reads). Here the
+        # two values are on the host, so a kv_start the kernel would read out of bounds with is refused.
+        if host["cu_kv"].numel() < 2 or host["cu_src"].numel() < 2:
+            raise ValueError("cu_kv and cu_src need two values each")
         rows = (int(host["cu_kv"][0]), int(host["cu_src"][1]))
+        pm = min(layer[0].shape[0] for layer in kv)
+        if not 0 <= rows[0] <= pm or rows[1] < 1:
+            raise ValueError(f"kv_start={rows[0]} must be in 0..{pm} and S={rows[1]} at least 1")
         plan = b.get("plan")
         if plan is None or plan["seen"] != seen or plan["rows"] != rows:
             # the copy lists for these host tensors and row ranges, as library-call arguments built

@@ -139,3 +139,27 @@ def test_run_from_host_copies_only_the_rows_read(full):
         small = sum(t.numel() * t.element_size() for t in (x, mods, dt, st["cu_kv"], st["cu_src"], *st["sa_pe"], *st["ca_pe"]))
         PM, kv0, S = st["mem_kv"][0][0].shape[0], int(st["cu_kv"][0]), int(st["cu_src"][1])
         assert mk.last_h2d_bytes == small + dims.L * 2 * row_bytes * ((PM - kv0) + S) + 4 * dims.L
+
+
+def test_run_from_host_refuses_out_of_range_row_limits(full):
+    """kv_start and S are on the host here: a kv_start outside [0, PM] (the kernel would read outside
+    the memory) or S < 1 is refused before anything is copied or launched."""
+    dims, mk = full
+    inp = make_inputs(dims, seed=40)
+    args = (inp.x[:1].contiguous().pin_memory(), inp.mods[0].contiguous().pin_memory(),
+            inp.dt[:1].contiguous().pin_memory())
+    for kv0, S in ((-1, 160), (97, 160), (32, 0)):
+        hp = _pinned_past(inp)
+        hp.register_step["cu_kv"][0] = kv0
+        hp.register_step["cu_src"][1] = S
+        with pytest.raises(ValueError):
+            mk.run_from_host(*args, hp, inp.action_dim)
+    hp = _pinned_past(inp)
+    hp.register_step["cu_src"] = hp.register_step["cu_src"][:1].clone().pin_memory()
+    with pytest.raises(ValueError):
+        mk.run_from_host(*args, hp, inp.action_dim)
+    good = mk.run_from_host(*args, _pinned_past(inp), inp.action_dim)  # the handle still works
+    torch.cuda.synchronize()
+    mk.check_device_error()
+    d = inp.to(DEV)
+    assert torch.equal(good, mk.run(d.x[:1], d.mods[0], d.dt[:1], make_past(d), d.action_dim))
