@@ -8,12 +8,13 @@ from predict to predict (``_register_cache.append_frame``, src/profile_breakdown
 code is absent from the reference checkout; the parts here restate it (parity unpinned; the CPU
 restatement is ``oracle/register_oracle.py``):
 
-1. carry: the memory moves up by one frame (two device copies per K / V), the oldest frame drops;
+1. carry: the memory moves up by one frame (two device copies per K / V), the oldest frame drops
+   (a side branch of the graph beside ``RegisterPrepare``, joined before the register pass);
 2. ``RegisterPrepare``: every layer's cross-attention K/V from the VLM source rows (one tcgen05 launch);
 3. ``StepModulations``: the AdaRMS rows of all N steps (two launches, on a side branch of the graph
    that overlaps steps 1, 2 and 4);
 4. register pass (``BatchedExpert.register_pass``): the frame's R register rows through every layer
-   with plain norms, writing their K/V into the newest frame's memory rows (tcgen05 GEMMs, 12
+   with plain norms, writing their K/V into the newest frame's memory rows (tcgen05 GEMMs, 11
    launches per layer);
 5. the action rows: all N Euler steps in ONE persistent ``expert_kernel`` launch from the flow noise
    (the modulation rows behind a placeholder row 0, so the launch's steps 1..N read rows 1..N); step
@@ -80,6 +81,7 @@ class FullPredict:
             cross_attn_kv=[(self.k[l], self.v[l]) for l in range(L)])
         self.p = 0
         self.side = torch.cuda.Stream(dev)
+        self.carry = torch.cuda.Stream(dev)
         self.graph = None
         if graph:
             side = torch.cuda.Stream(dev)
@@ -101,10 +103,16 @@ class FullPredict:
         self.side.wait_stream(main)
         with torch.cuda.stream(self.side):
             self.modulations.run(self.N, self.state, out=(self.mods[1:], self.dt))
-        for m in (self.memk, self.memv):  # carry: frames move up by one, the oldest drops
-            self.tmp.copy_(m[:, R:])
-            m[:, :-R].copy_(self.tmp)
+        # the carry (frames move up by one, the oldest drops) on a second branch: register_prepare
+        # does not touch the memory, and its 120 CTAs leave SMs for the copies; joined before the
+        # register pass, which writes the newest frame
+        self.carry.wait_stream(main)
+        with torch.cuda.stream(self.carry):
+            for m in (self.memk, self.memv):
+                self.tmp.copy_(m[:, R:])
+                m[:, :-R].copy_(self.tmp)
         self.prepare.run(self.src, self.cos, self.sin, SP=self.k.shape[1], out=(self.k, self.v))
+        main.wait_stream(self.carry)
         self.batched.register_pass(self.reg_in, self.memk, self.memv, self.cu_kv[:1], self.k, self.v,
                                    self.cu_src[1:], self.reg_sa, self.reg_ca)
         main.wait_stream(self.side)
